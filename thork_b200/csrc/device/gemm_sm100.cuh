@@ -1,0 +1,332 @@
+// gemm_sm100.cuh — persistent, warp-specialised tcgen05 GEMM for sm_100a.
+//
+//   D[GM, GN] = alpha * (A . B),  fp32 accumulation in tensor memory (TMEM),
+//   bf16 output written row-major (or transposed, for the swap-AB skinny path).
+//
+// One CTA per SM loops over output tiles.  Warp roles (192 threads):
+//   warp 0    TMA producer: fills a STAGES-deep ring of shared-memory stages.
+//   warp 1    MMA issuer: allocates TMEM, issues tcgen05.mma (one thread) and
+//             tcgen05.commit to release stages / publish accumulators.
+//   warps 2-5 epilogue: tcgen05.ld TMEM -> registers -> bf16 -> 128-bit
+//             global stores; TMEM lane quadrant = warp_id % 4.
+// The accumulator is double-buffered in TMEM (2 x BN fp32 columns), so the
+// epilogue of tile i overlaps the main loop of tile i+1.
+//
+// Operand layouts in shared memory are the 128-byte-swizzled canonical
+// layouts that TMA (CU_TENSOR_MAP_SWIZZLE_128B) writes:
+//   K-major operand (row-major A[M,K]):  BM rows x 128 bytes of K.
+//   MN-major operand (row-major B[K,N]):  chunks of 128 bytes of N, each
+//     BK rows deep; chunk c at c * BK * 128 bytes.
+// BK is one 128-byte swizzle atom of K (64 bf16 or 128 e4m3 elements).
+#pragma once
+#include "sm100.cuh"
+
+namespace thork {
+namespace gemm {
+
+using namespace thork::dev;
+
+enum : int { KIND_BF16 = 0, KIND_E4M3 = 1 };
+
+__host__ __device__ constexpr int ceil_pow2_cols(int n) {
+  return n <= 32 ? 32 : n <= 64 ? 64 : n <= 128 ? 128 : n <= 256 ? 256 : 512;
+}
+
+template <int KIND_, int BN_, int STAGES_, bool A_MN_, bool B_MN_, bool TRANS_OUT_>
+struct Config {
+  static constexpr int KIND = KIND_;
+  static constexpr int ELEM = KIND == KIND_BF16 ? 2 : 1;  // bytes per operand element
+  static constexpr int BM = 128;                           // UMMA M (one CTA)
+  static constexpr int BN = BN_;                           // UMMA N
+  static constexpr int BK = 128 / ELEM;                    // one swizzle atom of K
+  static constexpr int UMMA_K = 32 / ELEM;                 // K per tcgen05.mma
+  static constexpr int CHUNK = 128 / ELEM;                 // MN elements per 128-byte chunk
+  static constexpr int STAGES = STAGES_;
+  static constexpr bool A_MN = A_MN_;
+  static constexpr bool B_MN = B_MN_;
+  static constexpr bool TRANS_OUT = TRANS_OUT_;
+  static constexpr int A_BYTES = BM * BK * ELEM;
+  static constexpr int B_BYTES = BN * BK * ELEM;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = ceil_pow2_cols(2 * BN);
+  static constexpr int THREADS = 192;
+  // stages + barriers (full/empty per stage, tmem full/empty x2, teardown) + tmem slot
+  static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+  static constexpr u32 IDESC =
+      make_idesc(KIND == KIND_BF16 ? 1u : 0u, KIND == KIND_BF16 ? 1u : 0u, A_MN, B_MN, BM, BN);
+
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N must be 16..256, multiple of 16");
+  static_assert(!A_MN || BM % CHUNK == 0, "MN-major A needs BM multiple of the 128-byte chunk");
+  static_assert(!B_MN || BN % CHUNK == 0, "MN-major B needs BN multiple of the 128-byte chunk");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
+};
+
+struct Params {
+  void *out;      // bf16 output
+  int GM, GN, GK; // MMA-space extents
+  int ldo;        // output leading dimension (elements)
+  int out_rows;   // rows of the output matrix (bounds for stores)
+  int out_cols;   // cols of the output matrix
+  float alpha;
+  u32 *status;
+};
+
+// Output-tile order: groups of GROUP_M tile-rows walked column by column, so
+// the ~SM-count tiles in flight share A rows and B columns in L2.
+__device__ __forceinline__ void tile_coords(int t, int ntm, int ntn, int &tm, int &tn) {
+  const int GROUP_M = 16;
+  const int per_group = GROUP_M * ntn;
+  const int g = t / per_group;
+  const int first = g * GROUP_M;
+  const int gsize = min(ntm - first, GROUP_M);
+  const int r = t - g * per_group;
+  tm = first + r % gsize;
+  tn = r / gsize;
+}
+
+template <class Cfg>
+__device__ __forceinline__ void load_operand(u32 dst, const TensorMap *tm, u32 bar, bool mn_major,
+                                             int extent, int mn0, int k0) {
+  if (mn_major) {
+    // global tensor is [K rows, MN cols]; one box per 128-byte MN chunk
+#pragma unroll
+    for (int c = 0; c < extent / Cfg::CHUNK; ++c)
+      tma_load_2d(dst + c * Cfg::BK * 128, tm, bar, mn0 + c * Cfg::CHUNK, k0);
+  } else {
+    // global tensor is [MN rows, K cols]; one box of extent rows x 128 bytes
+    tma_load_2d(dst, tm, bar, k0, mn0);
+  }
+}
+
+template <class Cfg>
+__device__ __forceinline__ u64 operand_desc(u32 base, bool mn_major, int kstep) {
+  if (mn_major) return smem_desc_sw128(base + kstep * Cfg::UMMA_K * 128, Cfg::BK * 128, 1024);
+  return smem_desc_sw128(base + kstep * 32, 16, 1024);
+}
+
+__device__ __forceinline__ void st_global_b16(void *p, u32 v) {
+  asm volatile("st.global.b16 [%0], %1;" ::"l"(p), "h"(static_cast<unsigned short>(v & 0xFFFFu))
+               : "memory");
+}
+
+// Epilogue for one accumulator row slice: TMEM lane row_mma of the tile,
+// columns [col0, col0 + BN) -> bf16.  Non-transposed output writes row
+// `row_mma` of D with 16-byte vector stores; transposed output (swap-AB
+// skinny path) writes column `row_mma` of D^T.
+template <class Cfg>
+__device__ __forceinline__ void bf16_store_tile(const Params &p, u32 t_row, int row_mma, int col0) {
+  constexpr int CH = (Cfg::BN % 32 == 0) ? 32 : 16;
+  unsigned short *out = static_cast<unsigned short *>(p.out);
+#pragma unroll 1
+  for (int c0 = 0; c0 < Cfg::BN; c0 += CH) {
+    u32 r[CH];
+    if constexpr (CH == 32)
+      tmem_ld_32x32b_x32(t_row + c0, r);
+    else
+      tmem_ld_32x32b_x16(t_row + c0, r);
+    tmem_wait_ld();
+    if (!Cfg::TRANS_OUT) {
+      if (row_mma < p.out_rows) {
+        unsigned short *dst = out + static_cast<long long>(row_mma) * p.ldo + col0 + c0;
+#pragma unroll
+        for (int j = 0; j < CH / 8; ++j) {
+          if (col0 + c0 + 8 * j < p.out_cols) {
+            u32 w[4];
+#pragma unroll
+            for (int h = 0; h < 4; ++h)
+              w[h] = pack_bf16x2(__uint_as_float(r[8 * j + 2 * h]) * p.alpha,
+                                 __uint_as_float(r[8 * j + 2 * h + 1]) * p.alpha);
+            st_global_v4(dst + 8 * j, w[0], w[1], w[2], w[3]);
+          }
+        }
+      }
+    } else {
+      if (row_mma < p.out_cols) {
+#pragma unroll
+        for (int i = 0; i < CH; ++i) {
+          const int orow = col0 + c0 + i;
+          if (orow < p.out_rows)
+            st_global_b16(out + static_cast<long long>(orow) * p.ldo + row_mma,
+                          pack_bf16x2(__uint_as_float(r[i]) * p.alpha, 0.0f));
+        }
+      }
+    }
+  }
+}
+
+template <class Cfg>
+__global__ void __launch_bounds__(192, 1)
+    gemm_kernel(const __grid_constant__ TensorMap tmap_a, const __grid_constant__ TensorMap tmap_b,
+                const Params p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // 1024-byte alignment for the 128-byte swizzle atoms
+  const u32 raw = smem_u32(smem_raw);
+  const u32 base = (raw + 1023u) & ~1023u;
+  unsigned char *smem = smem_raw + (base - raw);
+  const u32 stage0 = base;
+  const u32 bars = base + Cfg::STAGES * Cfg::STAGE_BYTES;
+  auto full_bar = [&](int s) { return bars + 8u * s; };
+  auto empty_bar = [&](int s) { return bars + 8u * (Cfg::STAGES + s); };
+  auto tfull_bar = [&](int a) { return bars + 8u * (2 * Cfg::STAGES + a); };
+  auto tempty_bar = [&](int a) { return bars + 8u * (2 * Cfg::STAGES + 2 + a); };
+  const u32 drain_bar = bars + 8u * (2 * Cfg::STAGES + 4);
+  u32 *tmem_slot = reinterpret_cast<u32 *>(smem + Cfg::STAGES * Cfg::STAGE_BYTES + (2 * Cfg::STAGES + 5) * 8);
+  volatile u32 *abort_flag = tmem_slot + 1;
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  const int ntm = (p.GM + Cfg::BM - 1) / Cfg::BM;
+  const int ntn = (p.GN + Cfg::BN - 1) / Cfg::BN;
+  const int ntiles = ntm * ntn;
+  const int nkb = (p.GK + Cfg::BK - 1) / Cfg::BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc<1>(smem_u32(tmem_slot), Cfg::TMEM_COLS);
+    tmem_relinquish<1>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const u32 tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int s = 0;
+      u32 ph = 0;
+      for (int t = blockIdx.x; t < ntiles && !*abort_flag; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(t, ntm, ntn, tm, tn);
+        const int m0 = tm * Cfg::BM, n0 = tn * Cfg::BN;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(empty_bar(s), ph ^ 1u, p.status, 1)) {
+            *abort_flag = 1;
+            break;
+          }
+          const u32 sa = stage0 + s * Cfg::STAGE_BYTES;
+          const u32 sb = sa + Cfg::A_BYTES;
+          mbar_arrive_expect_tx(full_bar(s), Cfg::STAGE_BYTES);
+          load_operand<Cfg>(sa, &tmap_a, full_bar(s), Cfg::A_MN, Cfg::BM, m0, kb * Cfg::BK);
+          load_operand<Cfg>(sb, &tmap_b, full_bar(s), Cfg::B_MN, Cfg::BN, n0, kb * Cfg::BK);
+          if (++s == Cfg::STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      // Drain: wait until every issued load has landed before the CTA may exit.
+      // The stage about to be reused was released by the MMA warp, so waiting
+      // on the empty barriers of the last STAGES slots covers every copy.
+      for (int i = 0; i < Cfg::STAGES; ++i) {
+        if (!mbar_wait(empty_bar(s), ph ^ 1u, p.status, 2)) break;
+        if (++s == Cfg::STAGES) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer
+    int s = 0;
+    u32 ph = 0;
+    int it = 0;
+    for (int t = blockIdx.x; t < ntiles && !*abort_flag; t += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const u32 acc_ph = (it >> 1) & 1;
+      const u32 d_tmem = tmem_base + acc * Cfg::BN;
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait(tempty_bar(acc), acc_ph ^ 1u, p.status, 3);
+      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (lane == 0) ok = mbar_wait(full_bar(s), ph, p.status, 4);
+        if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const u32 sa = stage0 + s * Cfg::STAGE_BYTES;
+          const u32 sb = sa + Cfg::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < Cfg::BK / Cfg::UMMA_K; ++k) {
+            const u64 ad = operand_desc<Cfg>(sa, Cfg::A_MN, k);
+            const u64 bd = operand_desc<Cfg>(sb, Cfg::B_MN, k);
+            const u32 accum = (kb > 0 || k > 0) ? 1u : 0u;
+            if (Cfg::KIND == KIND_BF16)
+              mma_f16_ss(d_tmem, ad, bd, Cfg::IDESC, accum);
+            else
+              mma_f8f6f4_ss(d_tmem, ad, bd, Cfg::IDESC, accum);
+          }
+          tc_commit(empty_bar(s));  // stage s free once these MMAs have read it
+        }
+        __syncwarp();
+        if (++s == Cfg::STAGES) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+      if (*abort_flag) break;
+      if (lane == 0) tc_commit(tfull_bar(acc));  // accumulator ready for the epilogue
+      __syncwarp();
+    }
+    // Teardown: make sure every MMA this thread issued has completed before
+    // TMEM is released.
+    if (lane == 0) {
+      tc_commit(drain_bar);
+      mbar_wait(drain_bar, 0, p.status, 5);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------ epilogue (warps 2..5)
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    int it = 0;
+    for (int t = blockIdx.x; t < ntiles && !*abort_flag; t += gridDim.x, ++it) {
+      int tm, tn;
+      tile_coords(t, ntm, ntn, tm, tn);
+      const int acc = it & 1;
+      const u32 acc_ph = (it >> 1) & 1;
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait(tfull_bar(acc), acc_ph, p.status, 6);
+      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int row_mma = tm * Cfg::BM + q * 32 + lane;  // MMA-space row owned by this thread
+      const u32 t_row = tmem_base + ((u32)(q * 32) << 16) + acc * Cfg::BN;
+      bf16_store_tile<Cfg>(p, t_row, row_mma, tn * Cfg::BN);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar(acc));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc<1>(tmem_base, Cfg::TMEM_COLS);
+}
+
+}  // namespace gemm
+}  // namespace thork

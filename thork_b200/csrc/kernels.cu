@@ -1,0 +1,314 @@
+// kernels.cu — the library kernels of libthork_rt.so and their C-ABI entry
+// points (declared in include/thork_rt.h):
+//   thork_matrix_add_f32    128-bit vectorised, grid-stride fp32 add
+//   thork_gemm_bf16         tcgen05 GEMM, bf16 x bf16 -> fp32 -> bf16
+//   thork_gemm_e4m3         tcgen05 GEMM, e4m3 x e4m3 -> fp32 -> scaled bf16
+//   thork_skinny_gemm_bf16  swap-AB tcgen05 GEMM for M <= 256 (decode shapes)
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <mutex>
+
+#include "device/gemm_sm100.cuh"
+#include "thork_internal.h"
+#include "thork_rt.h"
+
+using thork::dev::TensorMap;
+using thork::dev::u32;
+
+// ---------------------------------------------------------------------------
+// per-device state: status word, SM count, smem opt-in flags
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_dev_mu;
+unsigned *g_status[kMaxDevices] = {};
+int g_sms[kMaxDevices] = {};
+uint64_t g_smem_set[kMaxDevices] = {};  // bit i: kernel i has its smem attribute set
+
+int current_device(int *dev) {
+  cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return thork_cuda_error(e, "cudaGetDevice");
+  if (*dev < 0 || *dev >= kMaxDevices)
+    return thork_set_error(THORK_ERR_INVALID, "device index %d too large", *dev);
+  return THORK_OK;
+}
+}  // namespace
+
+int thork_status_word(unsigned **d_status) {
+  int dev, rc;
+  if ((rc = current_device(&dev))) return rc;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (!g_status[dev]) {
+    void *p = nullptr;
+    cudaError_t e = cudaMalloc(&p, 16);
+    if (e != cudaSuccess) return thork_cuda_error(e, "cudaMalloc(status word)");
+    e = cudaMemset(p, 0, 16);
+    if (e != cudaSuccess) return thork_cuda_error(e, "cudaMemset(status word)");
+    g_status[dev] = static_cast<unsigned *>(p);
+  }
+  *d_status = g_status[dev];
+  return THORK_OK;
+}
+
+int thork_sm_count(int *n) {
+  int dev, rc;
+  if ((rc = current_device(&dev))) return rc;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (!g_sms[dev]) {
+    cudaError_t e = cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return thork_cuda_error(e, "cudaDeviceGetAttribute(SM count)");
+  }
+  *n = g_sms[dev];
+  return THORK_OK;
+}
+
+static int ensure_smem(const void *kernel, int kernel_id, int bytes) {
+  int dev, rc;
+  if ((rc = current_device(&dev))) return rc;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (!(g_smem_set[dev] & (1ull << kernel_id))) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return thork_cuda_error(e, "cudaFuncSetAttribute(max dynamic smem)");
+    g_smem_set[dev] |= 1ull << kernel_id;
+  }
+  return THORK_OK;
+}
+
+extern "C" int thork_kernel_status(unsigned *status, int clear) {
+  if (!status) return thork_set_error(THORK_ERR_INVALID, "status is NULL");
+  unsigned *d;
+  int rc = thork_status_word(&d);
+  if (rc) return rc;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return thork_cuda_error(e, "cudaDeviceSynchronize");
+  e = cudaMemcpy(status, d, sizeof(unsigned), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return thork_cuda_error(e, "read status word");
+  if (clear) {
+    e = cudaMemset(d, 0, 16);
+    if (e != cudaSuccess) return thork_cuda_error(e, "clear status word");
+  }
+  return THORK_OK;
+}
+
+extern "C" int thork_status_pointer(void **d_status) {
+  if (!d_status) return thork_set_error(THORK_ERR_INVALID, "d_status is NULL");
+  unsigned *d;
+  int rc = thork_status_word(&d);
+  if (rc) return rc;
+  *d_status = d;
+  return THORK_OK;
+}
+
+static int launch_check(const char *what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return thork_cuda_error(e, what);
+  return THORK_OK;
+}
+
+// ---------------------------------------------------------------------------
+// elementwise add
+// ---------------------------------------------------------------------------
+// Each thread keeps 4 float4 loads of each input in flight per iteration;
+// loads and stores use the streaming (evict-first) cache policy because
+// every byte is touched once.
+__global__ void __launch_bounds__(256) add_f32_v4_kernel(float4 *__restrict__ out,
+                                                         const float4 *__restrict__ a,
+                                                         const float4 *__restrict__ b, size_t n4) {
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < n4; i += 4 * stride) {
+    float4 x[4], y[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      x[u] = __ldcs(a + i + u * stride);
+      y[u] = __ldcs(b + i + u * stride);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float4 r;
+      r.x = x[u].x + y[u].x;
+      r.y = x[u].y + y[u].y;
+      r.z = x[u].z + y[u].z;
+      r.w = x[u].w + y[u].w;
+      __stcs(out + i + u * stride, r);
+    }
+  }
+  for (; i < n4; i += stride) {
+    const float4 x = __ldcs(a + i), y = __ldcs(b + i);
+    float4 r;
+    r.x = x.x + y.x;
+    r.y = x.y + y.y;
+    r.z = x.z + y.z;
+    r.w = x.w + y.w;
+    __stcs(out + i, r);
+  }
+}
+
+// Scalar grid-stride add for the ragged tail and for unaligned pointers.
+__global__ void __launch_bounds__(256) add_f32_scalar_kernel(float *__restrict__ out,
+                                                             const float *__restrict__ a,
+                                                             const float *__restrict__ b, size_t n) {
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
+    out[i] = a[i] + b[i];
+}
+
+extern "C" int thork_matrix_add_f32(float *d_out, const float *d_a, const float *d_b, size_t n,
+                                    void *stream) {
+  if (n == 0) return THORK_OK;
+  if (!d_out || !d_a || !d_b) return thork_set_error(THORK_ERR_INVALID, "matrix_add: NULL pointer");
+  int sms, rc;
+  if ((rc = thork_sm_count(&sms))) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool aligned =
+      ((reinterpret_cast<uintptr_t>(d_out) | reinterpret_cast<uintptr_t>(d_a) |
+        reinterpret_cast<uintptr_t>(d_b)) & 15u) == 0;
+  const size_t n4 = aligned ? n / 4 : 0;
+  if (n4) {
+    // 8 resident 256-thread blocks per SM, fewer when the array is small.
+    size_t blocks = (n4 + 255) / 256;
+    const size_t cap = static_cast<size_t>(sms) * 8;
+    if (blocks > cap) blocks = cap;
+    add_f32_v4_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+        reinterpret_cast<float4 *>(d_out), reinterpret_cast<const float4 *>(d_a),
+        reinterpret_cast<const float4 *>(d_b), n4);
+    if ((rc = launch_check("add_f32_v4_kernel launch"))) return rc;
+  }
+  const size_t done = n4 * 4;
+  if (done < n) {
+    const size_t rest = n - done;
+    size_t blocks = (rest + 255) / 256;
+    const size_t cap = static_cast<size_t>(sms) * 8;
+    if (blocks > cap) blocks = cap;
+    add_f32_scalar_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(d_out + done, d_a + done,
+                                                                         d_b + done, rest);
+    if ((rc = launch_check("add_f32_scalar_kernel launch"))) return rc;
+  }
+  return THORK_OK;
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05 GEMMs
+// ---------------------------------------------------------------------------
+namespace {
+using namespace thork::gemm;
+
+// bf16 / e4m3 GEMM: A row-major [M,K] (K-major), B row-major [K,N] (MN-major)
+using CfgBf16 = Config<KIND_BF16, 256, 4, false, true, false>;
+using CfgE4m3 = Config<KIND_E4M3, 256, 4, false, true, false>;
+// skinny (swap-AB): A = W row-major [K,N] (MN-major), B = X row-major [M,K]
+// (K-major), output written transposed into Y[M,N].
+using CfgSkinny16 = Config<KIND_BF16, 16, 10, true, false, true>;
+using CfgSkinny32 = Config<KIND_BF16, 32, 10, true, false, true>;
+using CfgSkinny64 = Config<KIND_BF16, 64, 8, true, false, true>;
+using CfgSkinny128 = Config<KIND_BF16, 128, 6, true, false, true>;
+using CfgSkinny256 = Config<KIND_BF16, 256, 4, true, false, true>;
+
+enum KernelId { K_GEMM_BF16 = 0, K_GEMM_E4M3, K_SKINNY16, K_SKINNY32, K_SKINNY64, K_SKINNY128, K_SKINNY256 };
+
+template <class Cfg>
+int run_gemm(int kernel_id, const TensorMap &ta, const TensorMap &tb, const Params &prm,
+             cudaStream_t s, const char *name) {
+  int rc, sms;
+  auto kern = gemm_kernel<Cfg>;
+  if ((rc = ensure_smem(reinterpret_cast<const void *>(kern), kernel_id, Cfg::SMEM_BYTES))) return rc;
+  if ((rc = thork_sm_count(&sms))) return rc;
+  const int ntiles = ((prm.GM + Cfg::BM - 1) / Cfg::BM) * ((prm.GN + Cfg::BN - 1) / Cfg::BN);
+  const int grid = ntiles < sms ? ntiles : sms;
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(ta, tb, prm);
+  return launch_check(name);
+}
+
+int check_dims(int M, int N, int K, int align, const char *what) {
+  if (M <= 0 || N <= 0 || K <= 0)
+    return thork_set_error(THORK_ERR_INVALID, "%s: dimensions must be positive (M=%d N=%d K=%d)",
+                           what, M, N, K);
+  if (K % align || N % align)
+    return thork_set_error(THORK_ERR_INVALID,
+                           "%s: K and N must be multiples of %d for 16-byte TMA row strides "
+                           "(M=%d N=%d K=%d)",
+                           what, align, M, N, K);
+  return THORK_OK;
+}
+
+int check_ptrs(const void *a, const void *b, const void *c, const char *what) {
+  if (!a || !b || !c) return thork_set_error(THORK_ERR_INVALID, "%s: NULL pointer", what);
+  if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+       reinterpret_cast<uintptr_t>(c)) & 15u)
+    return thork_set_error(THORK_ERR_INVALID, "%s: pointers must be 16-byte aligned", what);
+  return THORK_OK;
+}
+}  // namespace
+
+extern "C" int thork_gemm_bf16(const void *d_a, const void *d_b, void *d_c, int M, int N, int K,
+                               int variant, void *stream) {
+  int rc;
+  if ((rc = check_dims(M, N, K, 8, "gemm_bf16"))) return rc;
+  if ((rc = check_ptrs(d_a, d_b, d_c, "gemm_bf16"))) return rc;
+  if (variant < 0 || variant > 2)
+    return thork_set_error(THORK_ERR_INVALID, "gemm_bf16: unknown variant %d", variant);
+  alignas(64) TensorMap ta, tb;
+  using C = CfgBf16;
+  if ((rc = thork_encode_tmap_2d(&ta, THORK_DT_BF16, d_a, M, K, (uint64_t)K * 2, C::BM, C::BK, 128)))
+    return rc;
+  if ((rc = thork_encode_tmap_2d(&tb, THORK_DT_BF16, d_b, K, N, (uint64_t)N * 2, C::BK, C::CHUNK, 128)))
+    return rc;
+  unsigned *status;
+  if ((rc = thork_status_word(&status))) return rc;
+  Params prm{d_c, M, N, K, N, M, N, 1.0f, status};
+  return run_gemm<C>(K_GEMM_BF16, ta, tb, prm, static_cast<cudaStream_t>(stream), "gemm_bf16 launch");
+}
+
+extern "C" int thork_gemm_e4m3(const void *d_a, const void *d_b, void *d_c, int M, int N, int K,
+                               float scale_a, float scale_b, int variant, void *stream) {
+  int rc;
+  if ((rc = check_dims(M, N, K, 16, "gemm_e4m3"))) return rc;
+  if ((rc = check_ptrs(d_a, d_b, d_c, "gemm_e4m3"))) return rc;
+  if (variant < 0 || variant > 2)
+    return thork_set_error(THORK_ERR_INVALID, "gemm_e4m3: unknown variant %d", variant);
+  alignas(64) TensorMap ta, tb;
+  using C = CfgE4m3;
+  if ((rc = thork_encode_tmap_2d(&ta, THORK_DT_E4M3, d_a, M, K, (uint64_t)K, C::BM, C::BK, 128)))
+    return rc;
+  if ((rc = thork_encode_tmap_2d(&tb, THORK_DT_E4M3, d_b, K, N, (uint64_t)N, C::BK, C::CHUNK, 128)))
+    return rc;
+  unsigned *status;
+  if ((rc = thork_status_word(&status))) return rc;
+  Params prm{d_c, M, N, K, N, M, N, scale_a * scale_b, status};
+  return run_gemm<C>(K_GEMM_E4M3, ta, tb, prm, static_cast<cudaStream_t>(stream), "gemm_e4m3 launch");
+}
+
+namespace {
+template <class Cfg>
+int run_skinny(int kernel_id, const void *d_x, const void *d_w, void *d_y, int M, int N, int K,
+               cudaStream_t s) {
+  int rc;
+  alignas(64) TensorMap ta, tb;
+  // A operand = W [K, N] (MN-major), B operand = X [M, K] (K-major, rows >= M read as zero)
+  if ((rc = thork_encode_tmap_2d(&ta, THORK_DT_BF16, d_w, K, N, (uint64_t)N * 2, Cfg::BK, Cfg::CHUNK, 128)))
+    return rc;
+  if ((rc = thork_encode_tmap_2d(&tb, THORK_DT_BF16, d_x, M, K, (uint64_t)K * 2, Cfg::BN, Cfg::BK, 128)))
+    return rc;
+  unsigned *status;
+  if ((rc = thork_status_word(&status))) return rc;
+  // MMA space: GM = N (W columns), GN = M (X rows); output Y [M, N] written transposed.
+  Params prm{d_y, N, M, K, N, M, N, 1.0f, status};
+  return run_gemm<Cfg>(kernel_id, ta, tb, prm, s, "skinny_gemm_bf16 launch");
+}
+}  // namespace
+
+extern "C" int thork_skinny_gemm_bf16(const void *d_x, const void *d_w, void *d_y, int M, int N,
+                                      int K, void *stream) {
+  int rc;
+  if ((rc = check_dims(M, N, K, 8, "skinny_gemm_bf16"))) return rc;
+  if ((rc = check_ptrs(d_x, d_w, d_y, "skinny_gemm_bf16"))) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (M <= 16) return run_skinny<CfgSkinny16>(K_SKINNY16, d_x, d_w, d_y, M, N, K, s);
+  if (M <= 32) return run_skinny<CfgSkinny32>(K_SKINNY32, d_x, d_w, d_y, M, N, K, s);
+  if (M <= 64) return run_skinny<CfgSkinny64>(K_SKINNY64, d_x, d_w, d_y, M, N, K, s);
+  if (M <= 128) return run_skinny<CfgSkinny128>(K_SKINNY128, d_x, d_w, d_y, M, N, K, s);
+  if (M <= 256) return run_skinny<CfgSkinny256>(K_SKINNY256, d_x, d_w, d_y, M, N, K, s);
+  return thork_set_error(THORK_ERR_INVALID, "skinny_gemm_bf16: M must be <= 256 (M=%d)", M);
+}

@@ -1,0 +1,112 @@
+"""``tk.kernels.matmul(M, N, K, dtype)``: ``out = A @ B`` (row-major).
+
+Drop-in for the reference's ``src/thork/kernels/matmul.py:17-71`` (a 16x16
+shared-memory SIMT kernel, float32 only).  Routing by dtype:
+
+* ``float32``: a traced shared-memory-tiled SIMT kernel (API parity; M, N, K
+  multiples of 16 like the reference).
+* ``bfloat16``: the tcgen05 GEMM ``thork_gemm_bf16`` (TMA, mbarrier pipeline,
+  TMEM accumulators), or for M <= 256 the swap-AB decode kernel
+  ``thork_skinny_gemm_bf16``.  Output bf16, fp32 accumulation.
+* ``float8_e4m3``: ``thork_gemm_e4m3``; call as ``k(out, A, B, scale_a,
+  scale_b)`` with per-tensor scales, output bf16 = scale_a*scale_b*(A@B).
+
+Arguments are ``(out, A, B)`` like the reference.  bf16 arrays may be
+``ml_dtypes.bfloat16`` or raw ``uint16``; e4m3 arrays ``float8_e4m3fn`` or
+``uint8``.
+"""
+
+from .. import dtypes as dt
+from .. import runtime as rt
+from ..jit import jit
+from ..tracer import local, range as tk_range, shared, syncthreads
+from ..types import BlockIdx, DevicePointer, ThreadIdx, Uint2
+from ._library import ArgSpec, LibraryKernel
+
+_TILE = 16
+
+
+def _simt_matmul(M: int, N: int, K: int, dtype: dt.Dtype):
+    if M % _TILE or N % _TILE or K % _TILE:
+        raise ValueError(
+            f"matmul: M, N, K must all be multiples of {_TILE}; got M={M}, N={N}, K={K}")
+
+    @jit
+    def matmul_kernel(
+        out: DevicePointer[dtype],
+        A: DevicePointer[dtype],
+        B: DevicePointer[dtype],
+        bid: Uint2[BlockIdx],
+        tid: Uint2[ThreadIdx],
+    ):
+        a_s = shared(dtype, (_TILE, _TILE))
+        b_s = shared(dtype, (_TILE, _TILE))
+        r = bid.y * _TILE + tid.y
+        c = bid.x * _TILE + tid.x
+        acc = local(dtype, 0.0)
+        for k0 in tk_range(0, K, _TILE):
+            a_s[tid.y, tid.x] = A[r * K + k0 + tid.x]
+            b_s[tid.y, tid.x] = B[(k0 + tid.y) * N + c]
+            syncthreads()
+            for kk in tk_range(_TILE):
+                acc += a_s[tid.y, kk] * b_s[kk, tid.x]
+            syncthreads()
+        out[r * N + c] = acc
+
+    return matmul_kernel.bind(grid=(N // _TILE, M // _TILE, 1), block=(_TILE, _TILE, 1))
+
+
+def matmul(M: int, N: int, K: int, dtype: dt.Dtype = dt.float32, variant: str = "auto"):
+    """Return a kernel ``k(out, A, B)`` for ``out[M,N] = A[M,K] @ B[K,N]``.
+
+    ``variant`` (bf16 only): ``"auto"``, ``"gemm"`` (128x256 tcgen05 tiles),
+    ``"gemm2"`` (2-CTA 256x256 tiles) or ``"skinny"`` (swap-AB, M <= 256).
+    """
+    M, N, K = int(M), int(N), int(K)
+    if dtype == dt.float32:
+        return _simt_matmul(M, N, K, dtype)
+    if M <= 0 or N <= 0 or K <= 0:
+        raise ValueError(f"matmul: dimensions must be positive; got M={M}, N={N}, K={K}")
+    if dtype == dt.bfloat16:
+        if K % 8 or N % 8:
+            raise ValueError(f"matmul(bf16): K and N must be multiples of 8; got N={N}, K={K}")
+        if variant == "auto":
+            variant = "skinny" if M <= 256 else "gemm"
+        specs = [ArgSpec("out", dt.bfloat16, M * N, written=True, overwrites=True),
+                 ArgSpec("A", dt.bfloat16, M * K), ArgSpec("B", dt.bfloat16, K * N)]
+        if variant == "skinny":
+            if M > 256:
+                raise ValueError(f"matmul(bf16, skinny): M must be <= 256, got {M}")
+
+            def launch(p, s):
+                return rt.lib().thork_skinny_gemm_bf16(p[1], p[2], p[0], M, N, K, s)
+
+            name = "skinny_gemm_bf16"
+        elif variant in ("gemm", "gemm2"):
+            code = 1 if variant == "gemm" else 2
+
+            def launch(p, s):
+                return rt.lib().thork_gemm_bf16(p[1], p[2], p[0], M, N, K, code, s)
+
+            name = "gemm_bf16"
+        else:
+            raise ValueError(f"matmul: unknown variant {variant!r}")
+        return LibraryKernel(name, specs, launch, source=f"libthork_rt.so: thork_{name}")
+    if dtype == dt.float8_e4m3:
+        if K % 16 or N % 16:
+            raise ValueError(f"matmul(e4m3): K and N must be multiples of 16; got N={N}, K={K}")
+        specs = [ArgSpec("out", dt.bfloat16, M * N, written=True, overwrites=True),
+                 ArgSpec("A", dt.float8_e4m3, M * K), ArgSpec("B", dt.float8_e4m3, K * N)]
+
+        class _Fp8(LibraryKernel):
+            def __call__(self, out, A, B, scale_a=1.0, scale_b=1.0, stream=None, sync=True):
+                sa, sb = float(scale_a), float(scale_b)
+
+                def launch(p, s):
+                    return rt.lib().thork_gemm_e4m3(p[1], p[2], p[0], M, N, K, sa, sb, 0, s)
+
+                from ._library import run
+                run(self._specs, (out, A, B), launch, self._name, stream=stream, sync=sync)
+
+        return _Fp8("gemm_e4m3", specs, None, source="libthork_rt.so: thork_gemm_e4m3")
+    raise TypeError(f"matmul: unsupported dtype {dtype!r}")
