@@ -1,0 +1,662 @@
+"""Benchmark of the thork hot path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl thork|reference]
+
+For N > 1 launch one process per GPU with torch.distributed.run; torch is
+used here only for host-side plumbing (gloo barrier, max-over-ranks, NCCL
+unique-id broadcast) — the measured path is thork_b200 + libthork_rt.so.
+
+Workloads (default ``bf16_gemm_8192``):
+  bf16_gemm_8192  C = A.B, 8192^3 bf16, A split by contiguous rows over the N
+                  GPUs, B replicated, C all-gathered with NCCL (strong scaling)
+  bf16_gemm_4096  4096^3 bf16 (1 GPU config; rows split the same way at N > 1)
+  e4m3_gemm_8192  8192^3 FP8 e4m3 with per-tensor scales, bf16 out, gathered
+  skinny_m{1,16,128}  Y = X.W, K=4096, N=14336, bf16; W split by columns
+  add_f32         out = A + B over 2^28 fp32 elements (3 GiB of traffic);
+                  1024^2 (config 0) is reported under "also"
+
+A step is one pass of the hot path over one batch of synthetic input
+already resident in HBM (``value``).  ``e2e`` repeats the step through the
+public API (``tk.kernels.*`` / ``thork_b200.dist``) from pinned host buffers,
+host<->device copies included.  ``--impl reference`` times the reference's
+own CPU path (its NumPy verification arithmetic, restated in oracle/) on a
+bounded sample of the same workload, rank 0 only.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "bf16/fp8 GEMM TFLOP/s & % peak at 8192³; elementwise HBM GB/s; 1–8 GPUs"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+L2_BYTES = 126 * (1 << 20)
+
+
+# --------------------------------------------------------------------------
+# distributed plumbing
+# --------------------------------------------------------------------------
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+            import torch.distributed as tdist
+            tdist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+            self.tdist = tdist
+
+    def barrier(self):
+        if self.world > 1:
+            self.tdist.barrier()
+
+    def max(self, x: float) -> float:
+        if self.world == 1:
+            return x
+        import torch
+        t = torch.tensor([x], dtype=torch.float64)
+        self.tdist.all_reduce(t, op=self.tdist.ReduceOp.MAX)
+        return float(t.item())
+
+    def bcast_bytes(self, b):
+        if self.world == 1:
+            return b
+        obj = [b]
+        self.tdist.broadcast_object_list(obj, src=0)
+        return obj[0]
+
+    def close(self):
+        if self.world > 1:
+            self.tdist.destroy_process_group()
+
+
+# --------------------------------------------------------------------------
+# clocks during the timed region
+# --------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, local_rank: int):
+        cvd = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        ids = [x for x in cvd.split(",") if x.strip()]
+        self.index = ids[local_rank] if local_rank < len(ids) else str(local_rank)
+        self.samples = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", self.index],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append((time.perf_counter(), parts))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+
+    def summary(self, t0: float, t1: float):
+        inside = [p for t, p in self.samples if t0 <= t <= t1 + 0.25]
+        if not inside and self.samples:
+            inside = [min(self.samples, key=lambda s: abs(s[0] - (t0 + t1) / 2))[1]]
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+        sm = [num(p[1]) for p in inside if num(p[1]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for p in inside for n, v in zip(names, p[5:9]) if v.strip() == "Active"})
+        pw = [num(p[3]) for p in inside if num(p[3]) is not None]
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": num(inside[0][2]), "reasons": reasons,
+                "power_w_max": max(pw) if pw else None, "samples": len(inside)}
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {k: float(p[k]) for k in ("hbm_gbs", "bf16_tflops", "bf16_tflops_sustained")}, "measured"
+    except (OSError, KeyError, ValueError):
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+# --------------------------------------------------------------------------
+# workloads
+# --------------------------------------------------------------------------
+def bf16_bits(x):
+    from thork_b200 import dtypes
+    return dtypes.to_bf16_bits(x)
+
+
+class GemmWorkload:
+    """bf16 / e4m3 GEMM, rows of A split over ranks, C all-gathered."""
+
+    def __init__(self, size: int, kind: str, d: Dist, rt, dist_mod):
+        self.m = self.n = self.k = size
+        self.kind = kind
+        self.d = d
+        self.rt = rt
+        self.dist = dist_mod
+        self.start, self.stop = dist_mod.row_shard(self.m, d.world, d.rank)
+        self.m_loc = self.stop - self.start
+        rng = np.random.default_rng(0)
+        a = rng.standard_normal((self.m, self.k), dtype=np.float32)
+        b = rng.standard_normal((self.k, self.n), dtype=np.float32)
+        if kind == "bf16":
+            self.a_host = bf16_bits(a[self.start:self.stop])
+            self.b_host = bf16_bits(b)
+            self.scale = 1.0
+        else:
+            from thork_b200 import dtypes
+            # per-tensor scales of the full A and B (every rank draws the same
+            # inputs), then this rank's rows
+            qa, sa = dtypes.quantize_e4m3(a)
+            self.a_host = np.ascontiguousarray(qa[self.start:self.stop])
+            self.b_host, sb = dtypes.quantize_e4m3(b)
+            self.scale = float(sa) * float(sb)
+        del a, b
+        self.elem = self.a_host.dtype.itemsize
+        self.A = rt.DeviceArray.from_host(self.a_host)
+        self.B = rt.DeviceArray.from_host(self.b_host)
+        rows_out = self.m if d.world > 1 else self.m_loc
+        self.C = rt.empty((rows_out, self.n), np.uint16)
+        self.comm = None
+        if d.world > 1:
+            uid = None
+            if d.rank == 0:
+                import ctypes
+                buf = (ctypes.c_uint8 * 128)()
+                rt.check(rt.lib().thork_nccl_get_unique_id(buf))
+                uid = bytes(buf)
+            uid = d.bcast_bytes(uid)
+            self.comm = dist_mod.Communicator(d.rank, d.world, unique_id=uid)
+
+    flops_total = property(lambda self: 2.0 * self.m * self.n * self.k)
+    flops_local = property(lambda self: 2.0 * self.m_loc * self.n * self.k)
+
+    def step(self, stream, ev0=None, ev1=None):
+        if ev0 is not None:
+            ev0.record(stream)
+        self.dist.sharded_matmul(self.comm, self.A, self.B, self.C, self.m, dtype=self.kind,
+                                 scale=self.scale, gather=self.d.world > 1, stream=stream,
+                                 gemm_done=ev1)
+
+    def e2e_setup(self):
+        rt = self.rt
+        self.pa = rt.pinned_empty(self.a_host.shape, self.a_host.dtype)
+        self.pa[...] = self.a_host
+        self.pb = rt.pinned_empty(self.b_host.shape, self.b_host.dtype)
+        self.pb[...] = self.b_host
+        self.pc = rt.pinned_empty((self.m_loc, self.n), np.uint16)
+        self.h2d = self.pa.nbytes + self.pb.nbytes
+        self.d2h = self.pc.nbytes
+
+    def e2e_step(self, tk):
+        if self.d.world == 1:
+            dtype = tk.dt.bfloat16 if self.kind == "bf16" else tk.dt.float8_e4m3
+            mm = tk.kernels.matmul(self.m, self.n, self.k, dtype, variant="gemm") \
+                if self.kind == "bf16" else tk.kernels.matmul(self.m, self.n, self.k, dtype)
+            if self.kind == "bf16":
+                mm(self.pc, self.pa, self.pb)
+            else:
+                mm(self.pc, self.pa, self.pb, self.scale, 1.0)
+            return
+        self.dist.sharded_matmul_host(self.comm, self.pa, self.pb, self.pc, self.m,
+                                      dtype=self.kind, scale=self.scale)
+
+    def cpu_sample(self, seconds: float):
+        """The reference's check (NumPy fp32 matmul of the rounded inputs) on a
+        row sample of A; returns (TFLOP/s, sample description)."""
+        from oracle import oracle
+        if self.kind == "bf16":
+            a = oracle.bf16_bits_to_f32(self.a_host)
+            b = oracle.bf16_bits_to_f32(self.b_host)
+        else:
+            a = oracle.e4m3_bits_to_f32(self.a_host)
+            b = oracle.e4m3_bits_to_f32(self.b_host) * np.float32(self.scale)
+        return cpu_matmul_rate(a, b, seconds)
+
+
+def cpu_matmul_rate(a, b, seconds):
+    rows = 64
+    t = 0.0
+    while True:  # calibrate a sample of about 1 s
+        t0 = time.perf_counter()
+        _ = a[:rows] @ b
+        t = time.perf_counter() - t0
+        if t > 0.5 or rows >= a.shape[0]:
+            break
+        rows = min(a.shape[0], rows * 4)
+    reps = max(1, int(seconds / max(t, 1e-6)))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        _ = a[:rows] @ b
+    dt_s = time.perf_counter() - t0
+    flops = 2.0 * rows * a.shape[1] * b.shape[1] * reps
+    return flops / dt_s / 1e12, f"{reps} x ({rows}x{a.shape[1]} @ {a.shape[1]}x{b.shape[1]}) fp32 NumPy", rows
+
+
+class SkinnyWorkload:
+    """Decode GEMM Y = X.W (K=4096, N=14336); W split by columns over ranks,
+    three rotating copies of each W shard so no launch reads W from L2."""
+
+    def __init__(self, m: int, d: Dist, rt, dist_mod):
+        self.m, self.n, self.k = m, 14336, 4096
+        self.d, self.rt = d, rt
+        c0, c1 = dist_mod.col_shard(self.n, d.world, d.rank)
+        self.n_loc = c1 - c0
+        rng = np.random.default_rng(0)
+        w = rng.standard_normal((self.k, self.n), dtype=np.float32) * np.float32(0.02)
+        x = rng.standard_normal((m, self.k), dtype=np.float32)
+        self.x_host = bf16_bits(x)
+        self.w_host = np.ascontiguousarray(bf16_bits(w[:, c0:c1]))
+        self.X = rt.DeviceArray.from_host(self.x_host)
+        copies = max(3, int(np.ceil(3 * L2_BYTES / self.w_host.nbytes)))
+        self.W = [rt.DeviceArray.from_host(self.w_host) for _ in range(copies)]
+        self.Y = rt.empty((m, self.n_loc), np.uint16)
+        self.i = 0
+
+    bytes_local = property(lambda self: 2.0 * (self.k * self.n_loc + self.m * self.k + self.m * self.n_loc))
+    bytes_total = property(lambda self: 2.0 * (self.k * self.n + self.m * self.k * self.d.world + self.m * self.n))
+
+    def step(self, stream, ev0=None, ev1=None):
+        w = self.W[self.i % len(self.W)]
+        self.i += 1
+        if ev0 is not None:
+            ev0.record(stream)
+        self.rt.check(self.rt.lib().thork_skinny_gemm_bf16(
+            self.X.ptr, w.ptr, self.Y.ptr, self.m, self.n_loc, self.k, stream.handle))
+        if ev1 is not None:
+            ev1.record(stream)
+
+    def e2e_setup(self):
+        rt = self.rt
+        self.px = rt.pinned_empty(self.x_host.shape, np.uint16)
+        self.px[...] = self.x_host
+        self.pw = rt.pinned_empty(self.w_host.shape, np.uint16)
+        self.pw[...] = self.w_host
+        self.py = rt.pinned_empty((self.m, self.n_loc), np.uint16)
+        self.h2d = self.px.nbytes + self.pw.nbytes
+        self.d2h = self.py.nbytes
+
+    def e2e_step(self, tk):
+        tk.kernels.matmul(self.m, self.n_loc, self.k, tk.dt.bfloat16, variant="skinny")(
+            self.py, self.px, self.pw)
+
+    def cpu_sample(self, seconds):
+        from oracle import oracle
+        x = oracle.bf16_bits_to_f32(self.x_host)
+        w = oracle.bf16_bits_to_f32(self.w_host)
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < seconds:
+            _ = x @ w
+            reps += 1
+        dt_s = time.perf_counter() - t0
+        return self.bytes_local * reps / dt_s / 1e9, f"{reps} x ({self.m}x{self.k} @ {self.k}x{self.n_loc}) fp32 NumPy", None
+
+
+class AddWorkload:
+    """out = A + B over 2^28 fp32 elements, split by contiguous ranges."""
+
+    def __init__(self, n_total: int, d: Dist, rt, dist_mod):
+        self.n_total = n_total
+        s, e = dist_mod.row_shard(n_total, d.world, d.rank)
+        self.n = e - s
+        self.d, self.rt = d, rt
+        rng = np.random.default_rng(d.rank)
+        self.a_host = rng.standard_normal(self.n, dtype=np.float32)
+        self.b_host = rng.standard_normal(self.n, dtype=np.float32)
+        self.A = rt.DeviceArray.from_host(self.a_host)
+        self.B = rt.DeviceArray.from_host(self.b_host)
+        self.C = rt.empty((self.n,), np.float32)
+
+    bytes_local = property(lambda self: 12.0 * self.n)
+    bytes_total = property(lambda self: 12.0 * self.n_total)
+
+    def step(self, stream, ev0=None, ev1=None):
+        if ev0 is not None:
+            ev0.record(stream)
+        self.rt.check(self.rt.lib().thork_matrix_add_f32(self.C.ptr, self.A.ptr, self.B.ptr,
+                                                         self.n, stream.handle))
+        if ev1 is not None:
+            ev1.record(stream)
+
+    def e2e_setup(self):
+        rt = self.rt
+        self.pa = rt.pinned_empty((self.n,), np.float32)
+        self.pa[...] = self.a_host
+        self.pb = rt.pinned_empty((self.n,), np.float32)
+        self.pb[...] = self.b_host
+        self.pc = rt.pinned_empty((self.n,), np.float32)
+        self.h2d = self.pa.nbytes + self.pb.nbytes
+        self.d2h = self.pc.nbytes
+
+    def e2e_step(self, tk):
+        tk.kernels.matrix_add((self.n,))(self.pc, self.pa, self.pb)
+
+    def cpu_sample(self, seconds):
+        n = min(self.n, 1 << 26)
+        a, b = self.a_host[:n], self.b_host[:n]
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < seconds:
+            _ = a + b
+            reps += 1
+        dt_s = time.perf_counter() - t0
+        return 12.0 * n * reps / dt_s / 1e9, f"{reps} x NumPy a+b over {n} fp32", None
+
+
+def make_workload(name, d, rt, dist_mod):
+    if name == "bf16_gemm_8192":
+        return GemmWorkload(8192, "bf16", d, rt, dist_mod)
+    if name == "bf16_gemm_4096":
+        return GemmWorkload(4096, "bf16", d, rt, dist_mod)
+    if name == "e4m3_gemm_8192":
+        return GemmWorkload(8192, "e4m3", d, rt, dist_mod)
+    if name.startswith("skinny_m"):
+        return SkinnyWorkload(int(name[len("skinny_m"):]), d, rt, dist_mod)
+    if name == "add_f32":
+        return AddWorkload(1 << 28, d, rt, dist_mod)
+    raise SystemExit(f"unknown workload {name}")
+
+
+def describe(name, w, world):
+    if isinstance(w, GemmWorkload):
+        return {
+            "workload": name, "M": w.m, "N": w.n, "K": w.k,
+            "dtype_in": w.kind, "dtype_out": "bf16", "accumulate": "fp32",
+            "parallelism": (f"A rows split over {world} GPUs, B replicated, C all-gathered "
+                            "with NCCL" if world > 1 else "1 GPU"),
+            "l2_policy": "inputs+output larger than L2 (no flush needed)",
+        }, "TFLOP/s", "tensor"
+    if isinstance(w, SkinnyWorkload):
+        return {
+            "workload": name, "M": w.m, "N": w.n, "K": w.k, "dtype_in": "bf16",
+            "parallelism": (f"W columns split over {world} GPUs, X replicated, Y not gathered"
+                            if world > 1 else "1 GPU"),
+            "l2_policy": f"{len(w.W)} rotating copies of W (> 3x L2)",
+        }, "GB/s", "hbm"
+    return {"workload": name, "elements": w.n_total, "dtype_in": "fp32",
+            "parallelism": f"contiguous ranges over {world} GPUs" if world > 1 else "1 GPU",
+            "l2_policy": "3 GiB of traffic per step (> L2)"}, "GB/s", "hbm"
+
+
+def time_steps(w, rt, steps, warmup, d, per_launch_events=True):
+    s = rt.Stream()
+    for _ in range(warmup):
+        w.step(s)
+    s.synchronize()
+    evs = [(rt.Event(), rt.Event()) for _ in range(steps)] if per_launch_events else None
+    e0, e1 = rt.Event(), rt.Event()
+    rt.synchronize()
+    d.barrier()
+    t_wall0 = time.perf_counter()
+    e0.record(s)
+    for i in range(steps):
+        if evs:
+            w.step(s, evs[i][0], evs[i][1])
+        else:
+            w.step(s)
+    e1.record(s)
+    e1.synchronize()
+    t_wall1 = time.perf_counter()
+    total_ms = e0.elapsed_ms(e1)
+    kernel_ms = (sum(a.elapsed_ms(b) for a, b in evs) / steps) if evs else total_ms / steps
+    rt.synchronize()
+    d.barrier()
+    return total_ms, kernel_ms, t_wall0, t_wall1
+
+
+def run_thork(args, d: Dist):
+    import thork_b200 as tk
+    from thork_b200 import dist as dist_mod
+    rt = tk.runtime
+    rt.set_device(d.local_rank)
+    peaks, peak_src = load_peaks()
+    w = make_workload(args.workload, d, rt, dist_mod)
+    cfg, unit, bound = describe(args.workload, w, d.world)
+
+    sampler = ClockSampler(d.local_rank)
+    sampler.start()
+    total_ms, kernel_ms, tw0, tw1 = time_steps(w, rt, args.steps, args.warmup, d)
+    sampler.stop()
+    clocks = sampler.summary(tw0, tw1)
+    ms_step = d.max(total_ms / args.steps)
+
+    if unit == "TFLOP/s":
+        value = w.flops_total / (ms_step * 1e-3) / 1e12
+        achieved = w.flops_local / (kernel_ms * 1e-3) / 1e12
+        peak = peaks["bf16_tflops"] * (2.0 if w.kind == "e4m3" else 1.0)
+        peak_note = (f"{peak_src} bf16 burst" if w.kind == "bf16"
+                     else f"2 x {peak_src} bf16 burst (no measured FP8 peak)")
+        alg = f"2*M_local*N*K = {w.flops_local:.4g} FLOP per launch"
+    else:
+        value = w.bytes_total / (ms_step * 1e-3) / 1e9
+        achieved = w.bytes_local / (kernel_ms * 1e-3) / 1e9
+        peak = peaks["hbm_gbs"]
+        peak_note = f"{peak_src} HBM copy"
+        alg = f"{w.bytes_local:.4g} algorithmic bytes per launch"
+
+    # end to end through the public API, pinned host buffers, copies included
+    w.e2e_setup()
+    e2e_steps = max(2, min(args.steps, 10))
+    w.e2e_step(tk)
+    rt.synchronize()
+    d.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        w.e2e_step(tk)
+    e2e_s = d.max((time.perf_counter() - t0) / e2e_steps)
+    if unit == "TFLOP/s":
+        e2e_val = w.flops_total / e2e_s / 1e12
+    else:
+        e2e_val = w.bytes_total / e2e_s / 1e9
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": unit, "n_gpus": d.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": {"bf16_gemm_8192": "bf16", "bf16_gemm_4096": "bf16", "e4m3_gemm_8192": "e4m3"}.get(
+            args.workload, "bf16" if args.workload.startswith("skinny") else "f32"),
+        "data": "synthetic: seeded N(0,1) inputs (BASELINE shapes/distributions), host-rounded",
+        "config": cfg,
+        "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": round(peak, 1),
+                     "unit": unit.replace("TFLOP/s", "TFLOP/s"), "frac": round(achieved / peak, 4),
+                     "traffic": None, "peak_source": peak_note, "algorithmic": alg,
+                     "kernel_ms": round(kernel_ms, 5)},
+        "e2e": {"value": round(e2e_val, 3), "unit": unit, "h2d_bytes_per_step": int(w.h2d),
+                "d2h_bytes_per_step": int(w.d2h), "steps": e2e_steps,
+                "api": "tk.kernels.matmul/matrix_add" if d.world == 1 else "thork_b200.dist.sharded_matmul_host"},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+    if d.rank == 0 and d.world == 1:
+        v, sample, _ = w.cpu_sample(args.cpu_seconds)
+        line["cpu_baseline"] = {"value": round(v, 4), "unit": unit, "cores": os.cpu_count(),
+                                "kind": "port", "sample": sample,
+                                "threads": os.environ.get("OPENBLAS_NUM_THREADS", "all")}
+        if args.also:
+            line["also"] = also_measurements(args, d, rt, dist_mod, peaks)
+    traffic = traffic_from_profiles(args.workload)
+    if traffic is not None:
+        line["roofline"]["traffic"] = traffic
+    if w.__class__ is GemmWorkload and w.comm is not None:
+        w.comm.close()
+    if d.rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def also_measurements(args, d, rt, dist_mod, peaks):
+    """Short device-resident timings of the other BASELINE configs (1 GPU)."""
+    out = {}
+    for name, steps in (("e4m3_gemm_8192", 100), ("bf16_gemm_4096", 200), ("skinny_m1", 300),
+                        ("skinny_m16", 300), ("skinny_m128", 300), ("add_f32", 100)):
+        w = make_workload(name, d, rt, dist_mod)
+        total_ms, kernel_ms, _, _ = time_steps(w, rt, steps, 10, d, per_launch_events=False)
+        if isinstance(w, GemmWorkload):
+            v = w.flops_total / (kernel_ms * 1e-3) / 1e12
+            peak = peaks["bf16_tflops"] * (2.0 if w.kind == "e4m3" else 1.0)
+            out[name] = {"TFLOP/s": round(v, 1), "frac_of_peak": round(v / peak, 3),
+                         "ms": round(kernel_ms, 4)}
+        else:
+            v = w.bytes_total / (kernel_ms * 1e-3) / 1e9
+            out[name] = {"GB/s": round(v, 1), "frac_of_hbm": round(v / peaks["hbm_gbs"], 3),
+                         "us": round(kernel_ms * 1e3, 2)}
+        del w
+    # config 0: 1024 x 1024 fp32 add (12.6 MB, L2-resident; latency-bound)
+    a = rt.to_device(np.ones((1 << 20,), np.float32))
+    c = rt.empty((1 << 20,), np.float32)
+    s = rt.Stream()
+    e0, e1 = rt.Event(), rt.Event()
+    for _ in range(10):
+        rt.lib().thork_matrix_add_f32(c.ptr, a.ptr, a.ptr, 1 << 20, s.handle)
+    e0.record(s)
+    for _ in range(200):
+        rt.lib().thork_matrix_add_f32(c.ptr, a.ptr, a.ptr, 1 << 20, s.handle)
+    e1.record(s)
+    e1.synchronize()
+    us = e0.elapsed_ms(e1) / 200 * 1e3
+    out["add_f32_1024x1024"] = {"GB/s": round(12 * (1 << 20) / us / 1e3, 1), "us": round(us, 2),
+                                "note": "L2-resident, launch-latency bound"}
+    return out
+
+
+def traffic_from_profiles(workload):
+    """Per-launch DRAM bytes recorded from an ncu capture (profiles/*.json)."""
+    path = os.path.join(REPO, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(workload)
+    except (OSError, ValueError):
+        return None
+
+
+def run_reference(args, d: Dist):
+    """The reference's CPU path (NumPy verification arithmetic), rank 0 only."""
+    if d.rank != 0:
+        return
+    from oracle import oracle
+    name = args.workload
+    steps = args.steps + args.warmup
+    per_step = max(0.05, min(2.0, 90.0 / max(steps, 1)))
+    if name in ("bf16_gemm_8192", "bf16_gemm_4096", "e4m3_gemm_8192"):
+        size = 8192 if name.endswith("8192") else 4096
+        a, b = oracle.gemm_inputs(size, size, size, seed=0)
+        if name.startswith("e4m3"):
+            qa, sa = oracle.quantize_e4m3(a)
+            qb, sb = oracle.quantize_e4m3(b)
+            a = oracle.e4m3_bits_to_f32(qa) * sa
+            b = oracle.e4m3_bits_to_f32(qb) * sb
+        else:
+            a, b = oracle.round_bf16(a), oracle.round_bf16(b)
+        rate, _, rows = cpu_matmul_rate(a, b, per_step)
+        times = []
+        for i in range(steps):
+            t0 = time.perf_counter()
+            _ = a[:rows] @ b
+            times.append(time.perf_counter() - t0)
+        t = statistics.median(times[args.warmup:] or times)
+        value, unit = 2.0 * rows * size * size / t / 1e12, "TFLOP/s"
+        sample = f"rows 0..{rows} of A ({rows}x{size} @ {size}x{size}) fp32 NumPy per step"
+    elif name.startswith("skinny_m"):
+        m = int(name[len("skinny_m"):])
+        x, w = oracle.skinny_inputs(m, 14336, 4096, seed=0)
+        x, w = oracle.round_bf16(x), oracle.round_bf16(w)
+        times = []
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            _ = x @ w
+            times.append(time.perf_counter() - t0)
+        t = statistics.median(times[args.warmup:] or times)
+        value, unit = 2.0 * (4096 * 14336 + m * 4096 + m * 14336) / t / 1e9, "GB/s"
+        sample = f"full ({m}x4096 @ 4096x14336) fp32 NumPy per step"
+    else:
+        n = 1 << 26
+        a, b = oracle.add_inputs((n,), seed=0)
+        times = []
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            _ = oracle.add_ref(a, b)
+            times.append(time.perf_counter() - t0)
+        t = statistics.median(times[args.warmup:] or times)
+        value, unit = 12.0 * n / t / 1e9, "GB/s"
+        sample = f"NumPy a+b over {n} fp32 (2^26 of the 2^28 elements) per step"
+    cfg = {"workload": name, "parallelism": "host CPU (rank 0)",
+           "threads": os.environ.get("OPENBLAS_NUM_THREADS", "all cores")}
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": unit,
+        "n_gpus": d.world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(t * 1e3, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic: seeded N(0,1), host-rounded",
+        "config": cfg,
+        "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": os.cpu_count(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1500)
+    ap.add_argument("--warmup", type=int, default=30)
+    ap.add_argument("--workload", default="bf16_gemm_8192")
+    ap.add_argument("--impl", default="thork", choices=["thork", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-also", dest="also", action="store_false",
+                    help="omit the short timings of the other configs")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    d = Dist()
+    if d.world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE={d.world}", file=sys.stderr)
+    try:
+        if args.impl == "reference":
+            run_reference(args, d)
+        else:
+            run_thork(args, d)
+    finally:
+        d.close()
+
+
+if __name__ == "__main__":
+    main()

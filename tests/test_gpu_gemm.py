@@ -29,17 +29,22 @@ def _run_bf16(m, n, k, variant="auto", seed=0):
     return oracle.bf16_bits_to_f32(c16), ref
 
 
-@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (256, 256, 256), (200, 264, 136),
-                                   (1024, 512, 320), (384, 1280, 1024), (129, 8, 8)])
-def test_gemm_bf16_shapes(m, n, k):
-    c, ref = _run_bf16(m, n, k, variant="gemm")
+SHAPES = [(128, 256, 64), (256, 256, 256), (200, 264, 136), (1024, 512, 320), (384, 1280, 1024),
+          (129, 8, 8), (640, 384, 4096)]
+
+
+@pytest.mark.parametrize("variant", ["gemm", "gemm2"])
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_gemm_bf16_shapes(m, n, k, variant):
+    c, ref = _run_bf16(m, n, k, variant=variant)
     err = oracle.max_rel_err(c, ref)
     assert err <= TOL, f"max rel err {err:.3e}"
     assert np.isfinite(c).all()
 
 
-def test_gemm_bf16_config1_4096():
-    c, ref = _run_bf16(4096, 4096, 4096, variant="gemm")
+@pytest.mark.parametrize("variant", ["gemm", "gemm2"])
+def test_gemm_bf16_config1_4096(variant):
+    c, ref = _run_bf16(4096, 4096, 4096, variant=variant)
     err = oracle.max_rel_err(c, ref)
     assert err <= TOL, f"max rel err {err:.3e}"
     # the reference tests' own elementwise check, for information: every
@@ -47,11 +52,12 @@ def test_gemm_bf16_config1_4096():
     np.testing.assert_allclose(c, ref, atol=2e-1 * float(np.abs(ref).max()) / 64, rtol=2e-2)
 
 
-def test_gemm_bf16_repeatable_and_linear():
+@pytest.mark.parametrize("variant", ["gemm", "gemm2"])
+def test_gemm_bf16_repeatable_and_linear(variant):
     # determinism: same inputs, same bits; linearity: C(2A) == 2 C(A) exactly
     m = n = k = 512
     a16, b16 = _bf16_case(m, n, k, seed=4)
-    mm = tk.kernels.matmul(m, n, k, tk.dt.bfloat16, variant="gemm")
+    mm = tk.kernels.matmul(m, n, k, tk.dt.bfloat16, variant=variant)
     c1 = np.zeros((m, n), np.uint16)
     c2 = np.zeros((m, n), np.uint16)
     mm(c1, a16, b16)
@@ -63,23 +69,25 @@ def test_gemm_bf16_repeatable_and_linear():
     np.testing.assert_array_equal(oracle.bf16_bits_to_f32(c3), 2 * oracle.bf16_bits_to_f32(c1))
 
 
-def test_gemm_bf16_identity_exact():
+@pytest.mark.parametrize("variant", ["gemm", "gemm2"])
+def test_gemm_bf16_identity_exact(variant):
     # A @ I == A exactly (one nonzero product per output, exact in fp32)
     m, k = 300, 256
     a16, _ = _bf16_case(m, k, k, seed=9)
     eye = oracle.f32_to_bf16_bits(np.eye(k, dtype=np.float32))
     c = np.zeros((m, k), np.uint16)
-    tk.kernels.matmul(m, k, k, tk.dt.bfloat16, variant="gemm")(c, a16, eye)
+    tk.kernels.matmul(m, k, k, tk.dt.bfloat16, variant=variant)(c, a16, eye)
     np.testing.assert_array_equal(c, a16)
 
 
+@pytest.mark.parametrize("variant", ["gemm", "gemm2"])
 @pytest.mark.parametrize("m,n,k", [(512, 768, 1024), (300, 272, 160), (128, 256, 128)])
-def test_gemm_e4m3(m, n, k):
+def test_gemm_e4m3(m, n, k, variant):
     a, b = oracle.gemm_inputs(m, n, k, seed=1)
     qa, sa = oracle.quantize_e4m3(a)
     qb, sb = oracle.quantize_e4m3(b)
     c16 = np.zeros((m, n), np.uint16)
-    tk.kernels.matmul(m, n, k, tk.dt.float8_e4m3)(c16, qa, qb, sa, sb)
+    tk.kernels.matmul(m, n, k, tk.dt.float8_e4m3, variant=variant)(c16, qa, qb, sa, sb)
     ref = oracle.gemm_e4m3_ref(qa, sa, qb, sb)
     err = oracle.max_rel_err(oracle.bf16_bits_to_f32(c16), ref)
     assert err <= TOL, f"max rel err {err:.3e}"

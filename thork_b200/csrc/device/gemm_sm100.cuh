@@ -328,5 +328,237 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) tmem_dealloc<1>(tmem_base, Cfg::TMEM_COLS);
 }
 
+// ===========================================================================
+// 2-CTA variant: a cluster of two CTAs computes a 256 x BN tile with
+// tcgen05.mma.cta_group::2 (M = 256).  CTA rank r loads rows [128r, 128r+128)
+// of the A tile and columns [BN/2*r, BN/2*(r+1)) of the B tile into its own
+// shared memory (no multicast); both CTAs' TMA loads complete on the leader's
+// (rank 0) full barrier.  The leader's MMA thread reads both CTAs' operands
+// and writes each CTA's 128 accumulator rows into that CTA's TMEM; its
+// commits release the stage / publish the accumulator in both CTAs.
+// ===========================================================================
+template <int KIND_, int BN_, int STAGES_>
+struct Config2 {
+  static constexpr int KIND = KIND_;
+  static constexpr int ELEM = KIND == KIND_BF16 ? 2 : 1;
+  static constexpr int BM = 128;       // rows per CTA (pair tile: 256)
+  static constexpr int BN = BN_;       // pair tile columns (UMMA N)
+  static constexpr int BNH = BN / 2;   // B columns held per CTA
+  static constexpr int BK = 128 / ELEM;
+  static constexpr int UMMA_K = 32 / ELEM;
+  static constexpr int CHUNK = 128 / ELEM;
+  static constexpr int STAGES = STAGES_;
+  static constexpr int A_BYTES = BM * BK * ELEM;
+  static constexpr int B_BYTES = BNH * BK * ELEM;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // per CTA
+  static constexpr int TMEM_COLS = ceil_pow2_cols(2 * BN);
+  static constexpr int THREADS = 192;
+  static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+  static constexpr u32 IDESC =
+      make_idesc(KIND == KIND_BF16 ? 1u : 0u, KIND == KIND_BF16 ? 1u : 0u, false, true, 256, BN);
+  static_assert(BN % 32 == 0 && BN <= 256, "pair tile N must be a multiple of 32, at most 256");
+  static_assert(BNH % CHUNK == 0, "per-CTA B columns must be whole 128-byte chunks");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
+};
+
+// 2-D tiled load whose completion is counted on a barrier of the leader CTA
+// (cta_group::2 form; `bar_cluster` is a shared::cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(u32 dst, const TensorMap *m, u32 bar_cluster, int x,
+                                                 int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<u64>(m)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+
+template <class Cfg>
+__global__ void __launch_bounds__(192, 1)
+    gemm2_kernel(const __grid_constant__ TensorMap tmap_a, const __grid_constant__ TensorMap tmap_b,
+                 const Params p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const u32 raw = smem_u32(smem_raw);
+  const u32 base = (raw + 1023u) & ~1023u;
+  unsigned char *smem = smem_raw + (base - raw);
+  const u32 stage0 = base;
+  const u32 bars = base + Cfg::STAGES * Cfg::STAGE_BYTES;
+  auto full_bar = [&](int s) { return bars + 8u * s; };
+  auto empty_bar = [&](int s) { return bars + 8u * (Cfg::STAGES + s); };
+  auto tfull_bar = [&](int a) { return bars + 8u * (2 * Cfg::STAGES + a); };
+  auto tempty_bar = [&](int a) { return bars + 8u * (2 * Cfg::STAGES + 2 + a); };
+  const u32 drain_bar = bars + 8u * (2 * Cfg::STAGES + 4);
+  u32 *tmem_slot =
+      reinterpret_cast<u32 *>(smem + Cfg::STAGES * Cfg::STAGE_BYTES + (2 * Cfg::STAGES + 5) * 8);
+  volatile u32 *abort_flag = tmem_slot + 1;
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const u32 rank = cluster_ctarank();
+  const int pair = blockIdx.x / 2;
+  const int npairs = gridDim.x / 2;
+
+  const int ntm = (p.GM + 2 * Cfg::BM - 1) / (2 * Cfg::BM);
+  const int ntn = (p.GN + Cfg::BN - 1) / Cfg::BN;
+  const int ntiles = ntm * ntn;
+  const int nkb = (p.GK + Cfg::BK - 1) / Cfg::BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::STAGES; ++s) {
+      mbar_init(full_bar(s), 1);   // leader: its producer's arrive.expect_tx
+      mbar_init(empty_bar(s), 1);  // leader MMA thread's commit
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 8);  // 4 epilogue warps in each CTA (leader's copy used)
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc<2>(smem_u32(tmem_slot), Cfg::TMEM_COLS);
+    tmem_relinquish<2>();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers are initialised before any remote use
+  tc_fence_after();
+  const u32 tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int s = 0;
+      u32 ph = 0;
+      for (int t = pair; t < ntiles && !*abort_flag; t += npairs) {
+        int tm, tn;
+        tile_coords(t, ntm, ntn, tm, tn);
+        const int m0 = tm * 2 * Cfg::BM + rank * Cfg::BM;
+        const int n0 = tn * Cfg::BN + rank * Cfg::BNH;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(empty_bar(s), ph ^ 1u, p.status, 0x11)) {
+            *abort_flag = 1;
+            break;
+          }
+          const u32 sa = stage0 + s * Cfg::STAGE_BYTES;
+          const u32 sb = sa + Cfg::A_BYTES;
+          const u32 fb = mapa_cluster(full_bar(s), 0);
+          if (rank == 0) mbar_arrive_expect_tx(full_bar(s), 2 * Cfg::STAGE_BYTES);
+          tma_load_2d_pair(sa, &tmap_a, fb, kb * Cfg::BK, m0);
+#pragma unroll
+          for (int c = 0; c < Cfg::BNH / Cfg::CHUNK; ++c)
+            tma_load_2d_pair(sb + c * Cfg::BK * 128, &tmap_b, fb, n0 + c * Cfg::CHUNK, kb * Cfg::BK);
+          if (++s == Cfg::STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      for (int i = 0; i < Cfg::STAGES; ++i) {
+        if (!mbar_wait(empty_bar(s), ph ^ 1u, p.status, 0x12)) break;
+        if (++s == Cfg::STAGES) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer (leader CTA)
+    if (rank == 0) {
+      int s = 0;
+      u32 ph = 0;
+      int it = 0;
+      for (int t = pair; t < ntiles && !*abort_flag; t += npairs, ++it) {
+        const int acc = it & 1;
+        const u32 acc_ph = (it >> 1) & 1;
+        const u32 d_tmem = tmem_base + acc * Cfg::BN;
+        bool ok = true;
+        if (lane == 0) ok = mbar_wait(tempty_bar(acc), acc_ph ^ 1u, p.status, 0x13);
+        if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (lane == 0) ok = mbar_wait(full_bar(s), ph, p.status, 0x14);
+          if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
+            *abort_flag = 1;
+            break;
+          }
+          tc_fence_after();
+          if (lane == 0) {
+            const u32 sa = stage0 + s * Cfg::STAGE_BYTES;
+            const u32 sb = sa + Cfg::A_BYTES;
+#pragma unroll
+            for (int k = 0; k < Cfg::BK / Cfg::UMMA_K; ++k) {
+              const u64 ad = smem_desc_sw128(sa + k * 32, 16, 1024);
+              const u64 bd = smem_desc_sw128(sb + k * Cfg::UMMA_K * 128, Cfg::BK * 128, 1024);
+              const u32 accum = (kb > 0 || k > 0) ? 1u : 0u;
+              if (Cfg::KIND == KIND_BF16)
+                mma2_f16_ss(d_tmem, ad, bd, Cfg::IDESC, accum);
+              else
+                mma2_f8f6f4_ss(d_tmem, ad, bd, Cfg::IDESC, accum);
+            }
+            tc_commit2(mapa_cluster(empty_bar(s), 0));
+            tc_commit2(mapa_cluster(empty_bar(s), 1));
+          }
+          __syncwarp();
+          if (++s == Cfg::STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (*abort_flag) break;
+        if (lane == 0) {
+          tc_commit2(mapa_cluster(tfull_bar(acc), 0));
+          tc_commit2(mapa_cluster(tfull_bar(acc), 1));
+        }
+        __syncwarp();
+      }
+      if (lane == 0) {
+        tc_commit2(mapa_cluster(drain_bar, 0));
+        mbar_wait(drain_bar, 0, p.status, 0x15);
+      }
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    int it = 0;
+    for (int t = pair; t < ntiles && !*abort_flag; t += npairs, ++it) {
+      int tm, tn;
+      tile_coords(t, ntm, ntn, tm, tn);
+      const int acc = it & 1;
+      const u32 acc_ph = (it >> 1) & 1;
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait(tfull_bar(acc), acc_ph, p.status, 0x16);
+      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int row = tm * 2 * Cfg::BM + rank * Cfg::BM + q * 32 + lane;
+      const u32 t_row = tmem_base + ((u32)(q * 32) << 16) + acc * Cfg::BN;
+      bf16_store_tile<Config<Cfg::KIND, Cfg::BN, 1, false, true, false>>(p, t_row, row, tn * Cfg::BN);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0)
+          mbar_arrive(tempty_bar(acc));
+        else
+          mbar_arrive_cluster(tempty_bar(acc), 0);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the leader's MMAs into both TMEMs are complete
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc<2>(tmem_base, Cfg::TMEM_COLS);
+}
+
 }  // namespace gemm
 }  // namespace thork

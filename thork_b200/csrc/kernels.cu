@@ -198,6 +198,9 @@ using namespace thork::gemm;
 // bf16 / e4m3 GEMM: A row-major [M,K] (K-major), B row-major [K,N] (MN-major)
 using CfgBf16 = Config<KIND_BF16, 256, 4, false, true, false>;
 using CfgE4m3 = Config<KIND_E4M3, 256, 4, false, true, false>;
+// 2-CTA (cluster pair) variants: 256 x 256 tiles, 32 KiB stages per CTA
+using Cfg2Bf16 = Config2<KIND_BF16, 256, 6>;
+using Cfg2E4m3 = Config2<KIND_E4M3, 256, 6>;
 // skinny (swap-AB): A = W row-major [K,N] (MN-major), B = X row-major [M,K]
 // (K-major), output written transposed into Y[M,N].
 using CfgSkinny16 = Config<KIND_BF16, 16, 10, true, false, true>;
@@ -206,7 +209,10 @@ using CfgSkinny64 = Config<KIND_BF16, 64, 8, true, false, true>;
 using CfgSkinny128 = Config<KIND_BF16, 128, 6, true, false, true>;
 using CfgSkinny256 = Config<KIND_BF16, 256, 4, true, false, true>;
 
-enum KernelId { K_GEMM_BF16 = 0, K_GEMM_E4M3, K_SKINNY16, K_SKINNY32, K_SKINNY64, K_SKINNY128, K_SKINNY256 };
+enum KernelId {
+  K_GEMM_BF16 = 0, K_GEMM_E4M3, K_SKINNY16, K_SKINNY32, K_SKINNY64, K_SKINNY128, K_SKINNY256,
+  K_GEMM2_BF16, K_GEMM2_E4M3
+};
 
 template <class Cfg>
 int run_gemm(int kernel_id, const TensorMap &ta, const TensorMap &tb, const Params &prm,
@@ -218,6 +224,33 @@ int run_gemm(int kernel_id, const TensorMap &ta, const TensorMap &tb, const Para
   const int ntiles = ((prm.GM + Cfg::BM - 1) / Cfg::BM) * ((prm.GN + Cfg::BN - 1) / Cfg::BN);
   const int grid = ntiles < sms ? ntiles : sms;
   kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(ta, tb, prm);
+  return launch_check(name);
+}
+
+// Cluster-pair launch: grid = 2 x (pairs), cluster (2,1,1).
+template <class Cfg>
+int run_gemm2(int kernel_id, const TensorMap &ta, const TensorMap &tb, const Params &prm,
+              cudaStream_t s, const char *name) {
+  int rc, sms;
+  auto kern = gemm2_kernel<Cfg>;
+  if ((rc = ensure_smem(reinterpret_cast<const void *>(kern), kernel_id, Cfg::SMEM_BYTES))) return rc;
+  if ((rc = thork_sm_count(&sms))) return rc;
+  const int ntiles = ((prm.GM + 2 * Cfg::BM - 1) / (2 * Cfg::BM)) * ((prm.GN + Cfg::BN - 1) / Cfg::BN);
+  const int pairs = ntiles < sms / 2 ? ntiles : sms / 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, prm);
+  if (e != cudaSuccess) return thork_cuda_error(e, name);
   return launch_check(name);
 }
 
@@ -251,6 +284,7 @@ extern "C" int thork_gemm_bf16(const void *d_a, const void *d_b, void *d_c, int 
     return thork_set_error(THORK_ERR_INVALID, "gemm_bf16: unknown variant %d", variant);
   alignas(64) TensorMap ta, tb;
   using C = CfgBf16;
+  // both variants read A in 128 x BK boxes and B in BK x 64 boxes
   if ((rc = thork_encode_tmap_2d(&ta, THORK_DT_BF16, d_a, M, K, (uint64_t)K * 2, C::BM, C::BK, 128)))
     return rc;
   if ((rc = thork_encode_tmap_2d(&tb, THORK_DT_BF16, d_b, K, N, (uint64_t)N * 2, C::BK, C::CHUNK, 128)))
@@ -258,7 +292,10 @@ extern "C" int thork_gemm_bf16(const void *d_a, const void *d_b, void *d_c, int 
   unsigned *status;
   if ((rc = thork_status_word(&status))) return rc;
   Params prm{d_c, M, N, K, N, M, N, 1.0f, status};
-  return run_gemm<C>(K_GEMM_BF16, ta, tb, prm, static_cast<cudaStream_t>(stream), "gemm_bf16 launch");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (variant == 0) variant = (M >= 256) ? 2 : 1;
+  if (variant == 2) return run_gemm2<Cfg2Bf16>(K_GEMM2_BF16, ta, tb, prm, s, "gemm2_bf16 launch");
+  return run_gemm<C>(K_GEMM_BF16, ta, tb, prm, s, "gemm_bf16 launch");
 }
 
 extern "C" int thork_gemm_e4m3(const void *d_a, const void *d_b, void *d_c, int M, int N, int K,
@@ -277,7 +314,10 @@ extern "C" int thork_gemm_e4m3(const void *d_a, const void *d_b, void *d_c, int 
   unsigned *status;
   if ((rc = thork_status_word(&status))) return rc;
   Params prm{d_c, M, N, K, N, M, N, scale_a * scale_b, status};
-  return run_gemm<C>(K_GEMM_E4M3, ta, tb, prm, static_cast<cudaStream_t>(stream), "gemm_e4m3 launch");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (variant == 0) variant = (M >= 256) ? 2 : 1;
+  if (variant == 2) return run_gemm2<Cfg2E4m3>(K_GEMM2_E4M3, ta, tb, prm, s, "gemm2_e4m3 launch");
+  return run_gemm<C>(K_GEMM_E4M3, ta, tb, prm, s, "gemm_e4m3 launch");
 }
 
 namespace {

@@ -1,0 +1,194 @@
+"""Multi-GPU execution of the GEMM hot path: one process per GPU, NCCL over
+NVLink through libthork_rt.so (no reference counterpart: the reference
+hard-codes device 0, ``src/thork/runtime.py:85-105``).
+
+* ``Communicator`` — an NCCL communicator for this rank.  The 128-byte
+  unique id is created by rank 0 and exchanged through any key-value store
+  with ``set(key, bytes)`` / ``get(key) -> bytes`` (for example a
+  ``torch.distributed.TCPStore``); this module itself imports no torch.
+* ``row_shard`` / ``col_shard`` — the contiguous partitions used by the
+  sharded GEMMs.
+* ``sharded_matmul`` — each rank multiplies its contiguous M-row block of A
+  by the replicated B and, optionally, all-gathers C so every rank holds
+  the full row-major ``M x N`` result (the all-gather is the only
+  collective).
+* ``sharded_matmul_host`` — the same from host arrays (pinned for full
+  PCIe speed): this rank's A rows and B are copied in, C is gathered on the
+  devices and this rank's rows are copied back.
+* decode shapes split W by contiguous N-column blocks (``col_shard``) with X
+  replicated; gathered ``[G, M, N/G]`` blocks become ``M x N`` with
+  ``assemble_col_blocks``.
+"""
+
+import ctypes
+from typing import Callable, Optional, Tuple
+
+import numpy as np
+
+from . import runtime as rt
+
+DT_BF16 = 4
+DT_F32 = 3
+
+
+def row_shard(m: int, world: int, rank: int) -> Tuple[int, int]:
+    """Contiguous row range [start, stop) of ``rank`` when ``m`` rows are
+    split over ``world`` ranks (the first ``m % world`` ranks get one more)."""
+    if world < 1 or not (0 <= rank < world):
+        raise ValueError(f"rank {rank} out of range for world size {world}")
+    base, extra = divmod(m, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def col_shard(n: int, world: int, rank: int, align: int = 8) -> Tuple[int, int]:
+    """Contiguous column range of ``rank``; widths are multiples of ``align``
+    (16-byte TMA rows) except possibly the last."""
+    if n % align:
+        raise ValueError(f"N={n} must be a multiple of {align}")
+    s, e = row_shard(n // align, world, rank)
+    return s * align, e * align
+
+
+def assemble_col_blocks(gathered: np.ndarray, widths) -> np.ndarray:
+    """Turn all-gathered column blocks (concatenated ``[M, w_r]`` row-major
+    blocks, rank order) into one ``M x sum(w)`` row-major matrix."""
+    widths = list(widths)
+    total = sum(widths)
+    flat = gathered.reshape(-1)
+    m = flat.size // total
+    out = np.empty((m, total), gathered.dtype)
+    off = col = 0
+    for w in widths:
+        out[:, col:col + w] = flat[off:off + m * w].reshape(m, w)
+        off += m * w
+        col += w
+    return out
+
+
+class Communicator:
+    """An NCCL communicator for this process's rank (one GPU per process)."""
+
+    def __init__(self, rank: int, world: int, store=None, key: str = "thork_nccl_id",
+                 unique_id: Optional[bytes] = None):
+        rt.get_device()
+        self.rank, self.world = int(rank), int(world)
+        if unique_id is None:
+            if store is None:
+                raise ValueError("Communicator needs a store or a unique_id")
+            if self.rank == 0:
+                buf = (ctypes.c_uint8 * 128)()
+                rt.check(rt.lib().thork_nccl_get_unique_id(buf), "nccl unique id")
+                unique_id = bytes(buf)
+                store.set(key, unique_id)
+            else:
+                unique_id = bytes(store.get(key))
+        if len(unique_id) != 128:
+            raise ValueError("NCCL unique id must be 128 bytes")
+        uid = (ctypes.c_uint8 * 128).from_buffer_copy(unique_id)
+        h = ctypes.c_void_p()
+        rt.check(rt.lib().thork_nccl_comm_init_rank(ctypes.byref(h), self.world, uid, self.rank),
+                 "nccl comm init")
+        self.handle = h.value
+
+    def allgather(self, send_ptr: int, recv_ptr: int, count: int, dtype: int,
+                  stream: Optional[rt.Stream] = None) -> None:
+        """recv[r*count:(r+1)*count] = send of rank r (elements of ``dtype``)."""
+        rt.check(rt.lib().thork_nccl_allgather(send_ptr, recv_ptr, count, dtype, self.handle,
+                                               stream.handle if stream else None), "nccl allgather")
+
+    def allreduce_sum(self, ptr: int, count: int, dtype: int, stream: Optional[rt.Stream] = None):
+        rt.check(rt.lib().thork_nccl_allreduce_sum(ptr, count, dtype, self.handle,
+                                                   stream.handle if stream else None),
+                 "nccl allreduce")
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            rt.lib().thork_nccl_comm_destroy(self.handle)
+            self.handle = None
+
+
+def _gemm_launcher(dtype: str, m: int, n: int, k: int, scale: float = 1.0) -> Callable:
+    L = rt.lib()
+    if dtype == "bf16":
+        return lambda a, b, c, s: L.thork_gemm_bf16(a, b, c, m, n, k, 0, s)
+    if dtype == "e4m3":
+        return lambda a, b, c, s: L.thork_gemm_e4m3(a, b, c, m, n, k, float(scale), 1.0, 0, s)
+    raise ValueError(f"unknown GEMM dtype {dtype!r}")
+
+
+def sharded_matmul(comm: Optional[Communicator], a_local: "rt.DeviceArray", b: "rt.DeviceArray",
+                   c_out: "rt.DeviceArray", m_total: int, *, dtype: str = "bf16",
+                   scale: float = 1.0, gather: bool = True,
+                   stream: Optional[rt.Stream] = None, gemm_done: Optional[rt.Event] = None) -> None:
+    """This rank's share of ``C = A @ B`` with A split by contiguous rows.
+
+    ``a_local`` holds rows ``row_shard(m_total, world, rank)`` of A; ``b`` is
+    the full ``K x N`` matrix.  With ``gather`` the full ``m_total x N`` C is
+    all-gathered into ``c_out`` on every rank (rows must split evenly);
+    otherwise ``c_out`` receives this rank's rows only.  Queued on ``stream``.
+    """
+    world = comm.world if comm is not None else 1
+    rank = comm.rank if comm is not None else 0
+    start, stop = row_shard(m_total, world, rank)
+    m_loc = stop - start
+    k = a_local.shape[1]
+    n = b.shape[1]
+    if a_local.shape[0] != m_loc or b.shape[0] != k:
+        raise ValueError(f"shape mismatch: A rows {a_local.shape}, B {b.shape}, shard {m_loc}")
+    launch = _gemm_launcher(dtype, m_loc, n, k, scale)
+    sh = stream.handle if stream else None
+    if not gather or world == 1:
+        rt.check(launch(a_local.ptr, b.ptr, c_out.ptr, sh), "sharded gemm")
+        if gemm_done is not None:
+            gemm_done.record(stream)
+        return
+    if m_total % world:
+        raise ValueError(f"gather needs M={m_total} divisible by world size {world}")
+    # the local rows land in their final place inside the gathered buffer,
+    # and NCCL's in-place all-gather (send == recv + rank*count) fills the rest
+    offset = rank * m_loc * n * 2
+    rt.check(launch(a_local.ptr, b.ptr, c_out.ptr + offset, sh), "sharded gemm")
+    if gemm_done is not None:
+        gemm_done.record(stream)
+    comm.allgather(c_out.ptr + offset, c_out.ptr, m_loc * n, DT_BF16, stream)
+
+
+class _HostStaging:
+    """Device buffers reused across ``sharded_matmul_host`` calls."""
+
+    def __init__(self):
+        self.bufs = {}
+
+    def get(self, key, shape, dtype):
+        b = self.bufs.get(key)
+        if b is None or b.shape != tuple(shape) or b.dtype != np.dtype(dtype):
+            b = rt.empty(shape, dtype)
+            self.bufs[key] = b
+        return b
+
+
+_staging = _HostStaging()
+
+
+def sharded_matmul_host(comm: Optional[Communicator], a_rows: np.ndarray, b: np.ndarray,
+                        c_rows: np.ndarray, m_total: int, *, dtype: str = "bf16",
+                        scale: float = 1.0) -> None:
+    """Host-array form of ``sharded_matmul``: copies this rank's A rows and B
+    to the device, computes and all-gathers C on the devices, and copies this
+    rank's rows of C back into ``c_rows``.  Synchronous."""
+    stream = rt._dispatch_stream()
+    a_dev = _staging.get("a", a_rows.shape, a_rows.dtype)
+    b_dev = _staging.get("b", b.shape, b.dtype)
+    world = comm.world if comm is not None else 1
+    rows_out = m_total if world > 1 else a_rows.shape[0]
+    c_dev = _staging.get("c", (rows_out, b.shape[1]), np.uint16)
+    rt.copy_htod(a_dev.ptr, np.ascontiguousarray(a_rows), stream, sync=False)
+    rt.copy_htod(b_dev.ptr, np.ascontiguousarray(b), stream, sync=False)
+    sharded_matmul(comm, a_dev, b_dev, c_dev, m_total, dtype=dtype, scale=scale,
+                   gather=world > 1, stream=stream)
+    rank = comm.rank if comm is not None else 0
+    start, _ = row_shard(m_total, world, rank)
+    off = (start * b.shape[1] * 2) if world > 1 else 0
+    rt.copy_dtoh(c_rows, c_dev.ptr + off, stream, sync=False)
+    stream.synchronize()

@@ -88,3 +88,28 @@ def storage_compatible(arr_dtype, d: Dtype) -> bool:
     if d.name == "float8_e4m3":
         return arr_dtype == np.dtype(np.uint8)
     return False
+
+
+def to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """Round a float array to bf16 (nearest-even) and return the raw
+    ``uint16`` bit patterns, the storage the tile kernels consume."""
+    if _ml is None:  # pragma: no cover
+        raise RuntimeError("ml_dtypes is required for bf16 conversion")
+    return np.asarray(x, np.float32).astype(_ml.bfloat16).view(np.uint16)
+
+
+def from_bf16_bits(bits: np.ndarray) -> np.ndarray:
+    """Widen raw bf16 bit patterns (``uint16``) to float32."""
+    return (np.asarray(bits, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def quantize_e4m3(x: np.ndarray):
+    """Per-tensor FP8 quantisation: ``scale = amax / 448`` and the e4m3fn bytes
+    of ``x / scale`` (nearest-even).  Returns ``(uint8 array, float scale)``."""
+    if _ml is None:  # pragma: no cover
+        raise RuntimeError("ml_dtypes is required for e4m3 conversion")
+    x = np.asarray(x, np.float32)
+    amax = float(np.max(np.abs(x))) if x.size else 0.0
+    scale = np.float32(amax / 448.0) if amax > 0 else np.float32(1.0)
+    q = np.clip(x / scale, -448.0, 448.0).astype(_ml.float8_e4m3fn).view(np.uint8)
+    return q, float(scale)

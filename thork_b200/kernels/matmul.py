@@ -59,8 +59,9 @@ def _simt_matmul(M: int, N: int, K: int, dtype: dt.Dtype):
 def matmul(M: int, N: int, K: int, dtype: dt.Dtype = dt.float32, variant: str = "auto"):
     """Return a kernel ``k(out, A, B)`` for ``out[M,N] = A[M,K] @ B[K,N]``.
 
-    ``variant`` (bf16 only): ``"auto"``, ``"gemm"`` (128x256 tcgen05 tiles),
-    ``"gemm2"`` (2-CTA 256x256 tiles) or ``"skinny"`` (swap-AB, M <= 256).
+    ``variant``: ``"auto"``, ``"gemm"`` (128x256 tcgen05 tiles, one CTA),
+    ``"gemm2"`` (256x256 tiles on a 2-CTA cluster) or, bf16 only,
+    ``"skinny"`` (swap-AB, M <= 256).
     """
     M, N, K = int(M), int(N), int(K)
     if dtype == dt.float32:
@@ -71,7 +72,7 @@ def matmul(M: int, N: int, K: int, dtype: dt.Dtype = dt.float32, variant: str = 
         if K % 8 or N % 8:
             raise ValueError(f"matmul(bf16): K and N must be multiples of 8; got N={N}, K={K}")
         if variant == "auto":
-            variant = "skinny" if M <= 256 else "gemm"
+            variant = "skinny" if M <= 256 else "gemm2"
         specs = [ArgSpec("out", dt.bfloat16, M * N, written=True, overwrites=True),
                  ArgSpec("A", dt.bfloat16, M * K), ArgSpec("B", dt.bfloat16, K * N)]
         if variant == "skinny":
@@ -98,12 +99,16 @@ def matmul(M: int, N: int, K: int, dtype: dt.Dtype = dt.float32, variant: str = 
         specs = [ArgSpec("out", dt.bfloat16, M * N, written=True, overwrites=True),
                  ArgSpec("A", dt.float8_e4m3, M * K), ArgSpec("B", dt.float8_e4m3, K * N)]
 
+        code = {"auto": 0, "gemm": 1, "gemm2": 2}.get(variant)
+        if code is None:
+            raise ValueError(f"matmul: unknown variant {variant!r}")
+
         class _Fp8(LibraryKernel):
             def __call__(self, out, A, B, scale_a=1.0, scale_b=1.0, stream=None, sync=True):
                 sa, sb = float(scale_a), float(scale_b)
 
                 def launch(p, s):
-                    return rt.lib().thork_gemm_e4m3(p[1], p[2], p[0], M, N, K, sa, sb, 0, s)
+                    return rt.lib().thork_gemm_e4m3(p[1], p[2], p[0], M, N, K, sa, sb, code, s)
 
                 from ._library import run
                 run(self._specs, (out, A, B), launch, self._name, stream=stream, sync=sync)
