@@ -462,9 +462,14 @@ def run_thork(args, d: Dist):
     if unit == "TFLOP/s":
         value = w.flops_total / (ms_step * 1e-3) / 1e12
         achieved = w.flops_local / (kernel_ms * 1e-3) / 1e12
-        peak = peaks["bf16_tflops"] * (2.0 if w.kind == "e4m3" else 1.0)
-        peak_note = (f"{peak_src} bf16 burst" if w.kind == "bf16"
-                     else f"2 x {peak_src} bf16 burst (no measured FP8 peak)")
+        # a timed region over ~0.5 s runs under the 1 kW power cap: compare with
+        # the sustained cuBLAS figure; shorter regions with the burst figure
+        sustained = total_ms > 500.0
+        base_peak = peaks["bf16_tflops_sustained" if sustained else "bf16_tflops"]
+        kind = "sustained" if sustained else "burst"
+        peak = base_peak * (2.0 if w.kind == "e4m3" else 1.0)
+        peak_note = (f"{peak_src} bf16 {kind} (cuBLAS)" if w.kind == "bf16"
+                     else f"2 x {peak_src} bf16 {kind} (no measured FP8 peak)")
         alg = f"2*M_local*N*K = {w.flops_local:.4g} FLOP per launch"
     else:
         value = w.bytes_total / (ms_step * 1e-3) / 1e9

@@ -32,8 +32,9 @@ __host__ __device__ constexpr int ceil_pow2_cols(int n) {
   return n <= 32 ? 32 : n <= 64 ? 64 : n <= 128 ? 128 : n <= 256 ? 256 : 512;
 }
 
-template <int KIND_, int BN_, int STAGES_, bool A_MN_, bool B_MN_, bool TRANS_OUT_>
+template <int KIND_, int BN_, int STAGES_, bool A_MN_, bool B_MN_, bool TRANS_OUT_, int GROUP_M_ = 16>
 struct Config {
+  static constexpr int GROUP_M = GROUP_M_;  // tile rows per raster group
   static constexpr int KIND = KIND_;
   static constexpr int ELEM = KIND == KIND_BF16 ? 2 : 1;  // bytes per operand element
   static constexpr int BM = 128;                           // UMMA M (one CTA)
@@ -74,8 +75,8 @@ struct Params {
 
 // Output-tile order: groups of GROUP_M tile-rows walked column by column, so
 // the ~SM-count tiles in flight share A rows and B columns in L2.
+template <int GROUP_M>
 __device__ __forceinline__ void tile_coords(int t, int ntm, int ntn, int &tm, int &tn) {
-  const int GROUP_M = 16;
   const int per_group = GROUP_M * ntn;
   const int g = t / per_group;
   const int first = g * GROUP_M;
@@ -213,7 +214,7 @@ __global__ void __launch_bounds__(192, 1)
       u32 ph = 0;
       for (int t = blockIdx.x; t < ntiles && !*abort_flag; t += gridDim.x) {
         int tm, tn;
-        tile_coords(t, ntm, ntn, tm, tn);
+        tile_coords<Cfg::GROUP_M>(t, ntm, ntn, tm, tn);
         const int m0 = tm * Cfg::BM, n0 = tn * Cfg::BN;
         for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait(empty_bar(s), ph ^ 1u, p.status, 1)) {
@@ -303,7 +304,7 @@ __global__ void __launch_bounds__(192, 1)
     int it = 0;
     for (int t = blockIdx.x; t < ntiles && !*abort_flag; t += gridDim.x, ++it) {
       int tm, tn;
-      tile_coords(t, ntm, ntn, tm, tn);
+      tile_coords<Cfg::GROUP_M>(t, ntm, ntn, tm, tn);
       const int acc = it & 1;
       const u32 acc_ph = (it >> 1) & 1;
       bool ok = true;
@@ -337,8 +338,9 @@ __global__ void __launch_bounds__(192, 1)
 // and writes each CTA's 128 accumulator rows into that CTA's TMEM; its
 // commits release the stage / publish the accumulator in both CTAs.
 // ===========================================================================
-template <int KIND_, int BN_, int STAGES_>
+template <int KIND_, int BN_, int STAGES_, int GROUP_M_ = 16>
 struct Config2 {
+  static constexpr int GROUP_M = GROUP_M_;  // pair-tile rows per raster group
   static constexpr int KIND = KIND_;
   static constexpr int ELEM = KIND == KIND_BF16 ? 2 : 1;
   static constexpr int BM = 128;       // rows per CTA (pair tile: 256)
@@ -434,7 +436,7 @@ __global__ void __launch_bounds__(192, 1)
       u32 ph = 0;
       for (int t = pair; t < ntiles && !*abort_flag; t += npairs) {
         int tm, tn;
-        tile_coords(t, ntm, ntn, tm, tn);
+        tile_coords<Cfg::GROUP_M>(t, ntm, ntn, tm, tn);
         const int m0 = tm * 2 * Cfg::BM + rank * Cfg::BM;
         const int n0 = tn * Cfg::BN + rank * Cfg::BNH;
         for (int kb = 0; kb < nkb; ++kb) {
@@ -529,7 +531,7 @@ __global__ void __launch_bounds__(192, 1)
     int it = 0;
     for (int t = pair; t < ntiles && !*abort_flag; t += npairs, ++it) {
       int tm, tn;
-      tile_coords(t, ntm, ntn, tm, tn);
+      tile_coords<Cfg::GROUP_M>(t, ntm, ntn, tm, tn);
       const int acc = it & 1;
       const u32 acc_ph = (it >> 1) & 1;
       bool ok = true;
