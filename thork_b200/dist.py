@@ -66,6 +66,16 @@ def assemble_col_blocks(gathered: np.ndarray, widths) -> np.ndarray:
     return out
 
 
+def gather_slot(m_total: int, n: int, world: int, rank: int) -> Tuple[int, int]:
+    """(element offset, element count) of ``rank``'s rows inside the
+    gathered row-major ``m_total x n`` matrix; the all-gather needs equal
+    counts, so rows must split evenly."""
+    if m_total % world:
+        raise ValueError(f"gather needs M={m_total} divisible by world size {world}")
+    start, stop = row_shard(m_total, world, rank)
+    return start * n, (stop - start) * n
+
+
 class Communicator:
     """An NCCL communicator for this process's rank (one GPU per process)."""
 
@@ -143,15 +153,13 @@ def sharded_matmul(comm: Optional[Communicator], a_local: "rt.DeviceArray", b: "
         if gemm_done is not None:
             gemm_done.record(stream)
         return
-    if m_total % world:
-        raise ValueError(f"gather needs M={m_total} divisible by world size {world}")
     # the local rows land in their final place inside the gathered buffer,
     # and NCCL's in-place all-gather (send == recv + rank*count) fills the rest
-    offset = rank * m_loc * n * 2
-    rt.check(launch(a_local.ptr, b.ptr, c_out.ptr + offset, sh), "sharded gemm")
+    off_elems, count = gather_slot(m_total, n, world, rank)
+    rt.check(launch(a_local.ptr, b.ptr, c_out.ptr + 2 * off_elems, sh), "sharded gemm")
     if gemm_done is not None:
         gemm_done.record(stream)
-    comm.allgather(c_out.ptr + offset, c_out.ptr, m_loc * n, DT_BF16, stream)
+    comm.allgather(c_out.ptr + 2 * off_elems, c_out.ptr, count, DT_BF16, stream)
 
 
 class _HostStaging:

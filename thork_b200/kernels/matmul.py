@@ -72,7 +72,7 @@ def matmul(M: int, N: int, K: int, dtype: dt.Dtype = dt.float32, variant: str = 
         if K % 8 or N % 8:
             raise ValueError(f"matmul(bf16): K and N must be multiples of 8; got N={N}, K={K}")
         if variant == "auto":
-            variant = "skinny" if M <= 256 else "gemm2"
+            variant = "skinny" if M <= 256 else "gemm_auto"
         specs = [ArgSpec("out", dt.bfloat16, M * N, written=True, overwrites=True),
                  ArgSpec("A", dt.bfloat16, M * K), ArgSpec("B", dt.bfloat16, K * N)]
         if variant == "skinny":
@@ -83,8 +83,8 @@ def matmul(M: int, N: int, K: int, dtype: dt.Dtype = dt.float32, variant: str = 
                 return rt.lib().thork_skinny_gemm_bf16(p[1], p[2], p[0], M, N, K, s)
 
             name = "skinny_gemm_bf16"
-        elif variant in ("gemm", "gemm2"):
-            code = 1 if variant == "gemm" else 2
+        elif variant in ("gemm", "gemm2", "gemm_auto"):
+            code = {"gemm_auto": 0, "gemm": 1, "gemm2": 2}[variant]
 
             def launch(p, s):
                 return rt.lib().thork_gemm_bf16(p[1], p[2], p[0], M, N, K, code, s)
