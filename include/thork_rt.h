@@ -120,6 +120,9 @@ THORK_API int thork_event_destroy(void *event);
 THORK_API int thork_event_record(void *event, void *stream);
 THORK_API int thork_event_synchronize(void *event);
 THORK_API int thork_event_elapsed_ms(void *start, void *end, float *ms);
+/* Make `stream` wait for `event` (cross-stream ordering for the pipelined
+ * copy-in / compute / copy-out path).                                      */
+THORK_API int thork_stream_wait_event(void *stream, void *event);
 
 /* ---- NVRTC ---------------------------------------------------------- */
 /* NVRTC version linked at run time (dlopen of libnvrtc.so.12).            */

@@ -123,3 +123,23 @@ def test_gemm_bad_shapes_raise():
         tk.kernels.matmul(64, 100, 64, tk.dt.bfloat16)
     with pytest.raises(ValueError):
         tk.kernels.matmul(64, 64, 20, tk.dt.float8_e4m3)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "e4m3"])
+def test_pipelined_host_path_ragged_chunks(dtype):
+    # M = 3000 host arrays: row chunks of 512 (last 440) stream through
+    # copy-in / GEMM / copy-out on three streams
+    m, n, k = 3000, 512, 384
+    a, b = oracle.gemm_inputs(m, n, k, seed=11)
+    c16 = np.zeros((m, n), np.uint16)
+    if dtype == "bf16":
+        a16, b16 = oracle.f32_to_bf16_bits(a), oracle.f32_to_bf16_bits(b)
+        tk.kernels.matmul(m, n, k, tk.dt.bfloat16, variant="gemm")(c16, a16, b16)
+        ref = oracle.gemm_bf16_ref(a16, b16)
+    else:
+        qa, sa = oracle.quantize_e4m3(a)
+        qb, sb = oracle.quantize_e4m3(b)
+        tk.kernels.matmul(m, n, k, tk.dt.float8_e4m3)(c16, qa, qb, sa, sb)
+        ref = oracle.gemm_e4m3_ref(qa, sa, qb, sb)
+    err = oracle.max_rel_err(oracle.bf16_bits_to_f32(c16), ref)
+    assert err <= TOL, f"max rel err {err:.3e}"

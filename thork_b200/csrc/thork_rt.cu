@@ -275,6 +275,12 @@ extern "C" int thork_event_elapsed_ms(void *start, void *end, float *ms) {
   return THORK_OK;
 }
 
+extern "C" int thork_stream_wait_event(void *stream, void *event) {
+  CUDA_TRY(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), static_cast<cudaEvent_t>(event), 0),
+           "cudaStreamWaitEvent");
+  return THORK_OK;
+}
+
 // ---------------------------------------------------------------------------
 // NVRTC (dlopen)
 // ---------------------------------------------------------------------------

@@ -127,3 +127,61 @@ class LibraryKernel:
     @property
     def specs(self):
         return list(self._specs)
+
+
+class _Pipe:
+    """Per-thread streams for the pipelined host path."""
+
+    def __init__(self):
+        self.s_in = rt.Stream()
+        self.s_cmp = rt.Stream()
+        self.s_out = rt.Stream()
+
+
+_pipes = {}
+
+
+def _pipe() -> _Pipe:
+    import threading
+    key = (threading.get_ident(), rt.get_device())
+    p = _pipes.get(key)
+    if p is None:
+        p = _pipes[key] = _Pipe()
+    return p
+
+
+def run_rows_pipelined(a: np.ndarray, b: np.ndarray, c: np.ndarray, launch_rows, what: str,
+                       chunk_rows: int) -> None:
+    """``c = f(a, b)`` computed in row chunks of ``a``/``c`` with copy-in,
+    compute and copy-out on three streams, so host<->device transfers of one
+    chunk overlap the kernel of another.  ``launch_rows(a_ptr, b_ptr, c_ptr,
+    rows, stream)`` runs the kernel on ``rows`` rows and returns a status."""
+    ps = _pipe()
+    m = a.shape[0]
+    bufs = [rt.DeviceBuffer(x.nbytes) for x in (a, b, c)]
+    da, db, dc = (x.ptr for x in bufs)
+    a_row, c_row = a.nbytes // m, c.nbytes // m
+    events = []
+    try:
+        rt.copy_htod(db, b, ps.s_in, sync=False)
+        for r0 in range(0, m, chunk_rows):
+            r1 = min(m, r0 + chunk_rows)
+            ev_in, ev_done = rt.Event(), rt.Event()
+            events += [ev_in, ev_done]
+            rt.copy_htod(da + r0 * a_row, a[r0:r1], ps.s_in, sync=False)
+            ev_in.record(ps.s_in)
+            ps.s_cmp.wait(ev_in)
+            rt.check(launch_rows(da + r0 * a_row, db, dc + r0 * c_row, r1 - r0, ps.s_cmp.handle), what)
+            ev_done.record(ps.s_cmp)
+            ps.s_out.wait(ev_done)
+            rt.copy_dtoh(c[r0:r1], dc + r0 * c_row, ps.s_out, sync=False)
+        ps.s_out.synchronize()
+    finally:
+        for e in events:
+            e.close()
+        for x in bufs:
+            x.free()
+
+
+def is_host(*arrays) -> bool:
+    return all(isinstance(x, np.ndarray) for x in arrays)

@@ -21,7 +21,7 @@ from .. import runtime as rt
 from ..jit import jit
 from ..tracer import local, range as tk_range, shared, syncthreads
 from ..types import BlockIdx, DevicePointer, ThreadIdx, Uint2
-from ._library import ArgSpec, LibraryKernel
+from ._library import ArgSpec, LibraryKernel, _check_array, is_host, run, run_rows_pipelined
 
 _TILE = 16
 
@@ -54,6 +54,40 @@ def _simt_matmul(M: int, N: int, K: int, dtype: dt.Dtype):
         out[r * N + c] = acc
 
     return matmul_kernel.bind(grid=(N // _TILE, M // _TILE, 1), block=(_TILE, _TILE, 1))
+
+
+def _chunk_rows(m: int) -> int:
+    """Row-chunk size of the pipelined host path (multiples of 256 rows)."""
+    return max(256, ((m // 8) + 255) // 256 * 256)
+
+
+def _pipelinable(specs, args, m: int) -> bool:
+    """Host NumPy operands large enough that overlapping their transfers pays."""
+    if m < 1024 or not is_host(*args):
+        return False
+    for a, spec in zip(args, specs):
+        _check_array(a, spec)
+        if a.size != spec.count:
+            return False
+    return True
+
+
+class _GemmKernel(LibraryKernel):
+    """A GEMM whose NumPy-argument calls stream row chunks through
+    copy-in / tcgen05 GEMM / copy-out on three streams."""
+
+    def __init__(self, name, specs, launch, rows_launch, m, source=""):
+        super().__init__(name, specs, launch, source=source)
+        self._rows = rows_launch
+        self._m = m
+
+    def __call__(self, *args, stream=None, sync: bool = True):
+        if stream is None and len(args) == 3 and _pipelinable(self._specs, args, self._m):
+            rt.get_device()
+            out, a, b = args
+            run_rows_pipelined(a, b, out, self._rows, self._name, _chunk_rows(self._m))
+            return
+        super().__call__(*args, stream=stream, sync=sync)
 
 
 def matmul(M: int, N: int, K: int, dtype: dt.Dtype = dt.float32, variant: str = "auto"):
@@ -89,7 +123,11 @@ def matmul(M: int, N: int, K: int, dtype: dt.Dtype = dt.float32, variant: str = 
             def launch(p, s):
                 return rt.lib().thork_gemm_bf16(p[1], p[2], p[0], M, N, K, code, s)
 
-            name = "gemm_bf16"
+            def rows(a, b, c, m, s):
+                return rt.lib().thork_gemm_bf16(a, b, c, m, N, K, code, s)
+
+            return _GemmKernel("gemm_bf16", specs, launch, rows, M,
+                               source="libthork_rt.so: thork_gemm_bf16")
         else:
             raise ValueError(f"matmul: unknown variant {variant!r}")
         return LibraryKernel(name, specs, launch, source=f"libthork_rt.so: thork_{name}")
@@ -110,7 +148,13 @@ def matmul(M: int, N: int, K: int, dtype: dt.Dtype = dt.float32, variant: str = 
                 def launch(p, s):
                     return rt.lib().thork_gemm_e4m3(p[1], p[2], p[0], M, N, K, sa, sb, code, s)
 
-                from ._library import run
+                def rows(a, b, c, m, s):
+                    return rt.lib().thork_gemm_e4m3(a, b, c, m, N, K, sa, sb, code, s)
+
+                if stream is None and _pipelinable(self._specs, (out, A, B), M):
+                    rt.get_device()
+                    run_rows_pipelined(A, B, out, rows, self._name, _chunk_rows(M))
+                    return
                 run(self._specs, (out, A, B), launch, self._name, stream=stream, sync=sync)
 
         return _Fp8("gemm_e4m3", specs, None, source="libthork_rt.so: thork_gemm_e4m3")

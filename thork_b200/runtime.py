@@ -72,6 +72,7 @@ _SIGNATURES = {
     "thork_event_record": [_vp, _vp],
     "thork_event_synchronize": [_vp],
     "thork_event_elapsed_ms": [_vp, _vp, ctypes.POINTER(ctypes.c_float)],
+    "thork_stream_wait_event": [_vp, _vp],
     "thork_nvrtc_version": [ctypes.POINTER(_i), ctypes.POINTER(_i)],
     "thork_nvrtc_compile": [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p,
                             ctypes.POINTER(ctypes.c_char_p), _i, _pvp, ctypes.POINTER(_sz),
@@ -227,6 +228,10 @@ class Stream:
 
     def synchronize(self) -> None:
         check(lib().thork_stream_synchronize(self.handle), "stream synchronize")
+
+    def wait(self, event: "Event") -> None:
+        """Order later work on this stream after ``event``."""
+        check(lib().thork_stream_wait_event(self.handle, event.handle), "stream wait event")
 
     def close(self) -> None:
         if self.handle:
