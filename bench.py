@@ -518,7 +518,7 @@ def run_thork(args, d: Dist):
                                 "threads": os.environ.get("OPENBLAS_NUM_THREADS", "all")}
         if args.also:
             line["also"] = also_measurements(args, d, rt, dist_mod, peaks)
-    traffic = traffic_from_profiles(args.workload)
+    traffic = traffic_from_profiles(args.workload) if d.world == 1 else None
     if traffic is not None:
         line["roofline"]["traffic"] = traffic
     if w.__class__ is GemmWorkload and w.comm is not None:

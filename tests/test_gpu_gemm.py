@@ -143,3 +143,37 @@ def test_pipelined_host_path_ragged_chunks(dtype):
         ref = oracle.gemm_e4m3_ref(qa, sa, qb, sb)
     err = oracle.max_rel_err(oracle.bf16_bits_to_f32(c16), ref)
     assert err <= TOL, f"max rel err {err:.3e}"
+
+
+@pytest.mark.parametrize("m,n,k", [(20, 14336, 4096), (32, 1024, 512), (1, 4480, 512), (3, 128, 64),
+                                   (16, 2048, 8192)])
+def test_skinny_stream_k_shapes(m, n, k):
+    x, w = oracle.skinny_inputs(m, n, k, seed=5)
+    x16, w16 = oracle.f32_to_bf16_bits(x), oracle.f32_to_bf16_bits(w)
+    y16 = np.zeros((m, n), np.uint16)
+    tk.kernels.matmul(m, n, k, tk.dt.bfloat16, variant="skinny")(y16, x16, w16)
+    err = oracle.max_rel_err(oracle.bf16_bits_to_f32(y16), oracle.gemm_bf16_ref(x16, w16))
+    assert err <= TOL, f"max rel err {err:.3e}"
+
+
+def test_skinny_stream_k_repeated_calls_are_identical():
+    # the split tiles' arrival counters return to zero after every launch, so
+    # back-to-back calls (including a different shape in between) agree
+    m, n, k = 16, 14336, 4096
+    x, w = oracle.skinny_inputs(m, n, k, seed=6)
+    x16, w16 = oracle.f32_to_bf16_bits(x), oracle.f32_to_bf16_bits(w)
+    rt = tk.runtime
+    dx, dw = rt.to_device(x16), rt.to_device(w16)
+    dy = rt.empty((m, n), np.uint16)
+    mm = tk.kernels.matmul(m, n, k, tk.dt.bfloat16, variant="skinny")
+    outs = []
+    for i in range(3):
+        mm(dy, dx, dw)
+        outs.append(dy.to_host())
+        if i == 0:
+            other = np.zeros((8, 1024), np.uint16)
+            tk.kernels.matmul(8, 1024, 512, tk.dt.bfloat16, variant="skinny")(
+                other, x16[:8, :512].copy(), w16[:512, :1024].copy())
+    assert all(np.array_equal(outs[0], o) for o in outs[1:])
+    err = oracle.max_rel_err(oracle.bf16_bits_to_f32(outs[0]), oracle.gemm_bf16_ref(x16, w16))
+    assert err <= TOL

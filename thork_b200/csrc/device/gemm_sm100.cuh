@@ -160,6 +160,7 @@ template <class Cfg>
 __global__ void __launch_bounds__(192, 1)
     gemm_kernel(const __grid_constant__ TensorMap tmap_a, const __grid_constant__ TensorMap tmap_b,
                 const Params p) {
+  pdl_launch_dependents();
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 1024-byte alignment for the 128-byte swizzle atoms
   const u32 raw = smem_u32(smem_raw);
@@ -206,6 +207,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const u32 tmem_base = *tmem_slot;
+  pdl_wait();  // the previous kernel of the stream is complete from here on
 
   if (warp == 0) {
     // ------------------------------------------------ TMA producer
@@ -330,6 +332,281 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ===========================================================================
+// Stream-K decode GEMM (swap-AB skinny shapes).  The (tile, k-block) units of
+// the whole problem are split into gridDim.x contiguous, equal ranges, so
+// every SM streams the same share of W however few output tiles there are.
+// A tile covered by one CTA is stored directly; a tile split across CTAs has
+// each CTA write its fp32 partial to a workspace slot, and the CTA that
+// completes the tile's arrival counter sums the slots in slot order
+// (deterministic), writes the bf16 output and resets the counter to zero.
+// ===========================================================================
+struct SkParams {
+  Params p;
+  float *partial;       // [tiles][max_seg][BM][BN] fp32
+  unsigned *counters;   // [tiles], zero between launches
+  int base, extra;      // CTA c owns base + (c < extra) units
+  int max_seg;          // slots per tile in `partial`
+};
+
+__device__ __forceinline__ int sk_first_unit(int c, int base, int extra) {
+  return c * base + min(c, extra);
+}
+
+__device__ __forceinline__ int sk_cta_of_unit(int u, int base, int extra) {
+  const int big = extra * (base + 1);
+  return u < big ? u / (base + 1) : extra + (u - big) / base;
+}
+
+// Next tile segment [k0, k1) of this CTA's unit range; false when done.
+__device__ __forceinline__ bool sk_next(int &u, int end, int nkb, int &tile, int &k0, int &k1) {
+  if (u >= end) return false;
+  tile = u / nkb;
+  k0 = u - tile * nkb;
+  const int e = min(end, (tile + 1) * nkb);
+  k1 = k0 + (e - u);
+  u = e;
+  return true;
+}
+
+// Named barrier 1 over the 128 epilogue threads.
+__device__ __forceinline__ void epi_bar() {
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+// Same barrier, returning whether any of the 128 threads passed `v` = true,
+// so all epilogue warps take the same branch.
+__device__ __forceinline__ bool epi_vote_any(bool v) {
+  u32 r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.or.pred po, 1, 128, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"(v ? 1u : 0u)
+      : "memory");
+  return r != 0;
+}
+
+template <class Cfg>
+__global__ void __launch_bounds__(192, 1)
+    skinny_sk_kernel(const __grid_constant__ TensorMap tmap_a, const __grid_constant__ TensorMap tmap_b,
+                     const SkParams sp) {
+  pdl_launch_dependents();
+  static_assert(Cfg::A_MN && !Cfg::B_MN && Cfg::TRANS_OUT, "stream-K path is the swap-AB decode GEMM");
+  const Params &p = sp.p;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const u32 raw = smem_u32(smem_raw);
+  const u32 base = (raw + 1023u) & ~1023u;
+  unsigned char *smem = smem_raw + (base - raw);
+  const u32 stage0 = base;
+  const u32 bars = base + Cfg::STAGES * Cfg::STAGE_BYTES;
+  auto full_bar = [&](int s) { return bars + 8u * s; };
+  auto empty_bar = [&](int s) { return bars + 8u * (Cfg::STAGES + s); };
+  auto tfull_bar = [&](int a) { return bars + 8u * (2 * Cfg::STAGES + a); };
+  auto tempty_bar = [&](int a) { return bars + 8u * (2 * Cfg::STAGES + 2 + a); };
+  const u32 drain_bar = bars + 8u * (2 * Cfg::STAGES + 4);
+  u32 *tmem_slot = reinterpret_cast<u32 *>(smem + Cfg::STAGES * Cfg::STAGE_BYTES + (2 * Cfg::STAGES + 5) * 8);
+  volatile u32 *abort_flag = tmem_slot + 1;
+  volatile u32 *last_flag = tmem_slot + 2;
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int nkb = (p.GK + Cfg::BK - 1) / Cfg::BK;
+  const int u_begin = sk_first_unit(blockIdx.x, sp.base, sp.extra);
+  const int u_end = sk_first_unit(blockIdx.x + 1, sp.base, sp.extra);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc<1>(smem_u32(tmem_slot), Cfg::TMEM_COLS);
+    tmem_relinquish<1>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const u32 tmem_base = *tmem_slot;
+  pdl_wait();  // the previous kernel of the stream is complete from here on
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int s = 0;
+      u32 ph = 0;
+      int u = u_begin, tile, k0, k1;
+      while (!*abort_flag && sk_next(u, u_end, nkb, tile, k0, k1)) {
+        for (int kb = k0; kb < k1; ++kb) {
+          if (!mbar_wait(empty_bar(s), ph ^ 1u, p.status, 0x21)) {
+            *abort_flag = 1;
+            break;
+          }
+          const u32 sa = stage0 + s * Cfg::STAGE_BYTES;
+          const u32 sb = sa + Cfg::A_BYTES;
+          mbar_arrive_expect_tx(full_bar(s), Cfg::STAGE_BYTES);
+          load_operand<Cfg>(sa, &tmap_a, full_bar(s), true, Cfg::BM, tile * Cfg::BM, kb * Cfg::BK);
+          load_operand<Cfg>(sb, &tmap_b, full_bar(s), false, Cfg::BN, 0, kb * Cfg::BK);
+          if (++s == Cfg::STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      for (int i = 0; i < Cfg::STAGES; ++i) {
+        if (!mbar_wait(empty_bar(s), ph ^ 1u, p.status, 0x22)) break;
+        if (++s == Cfg::STAGES) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int s = 0;
+      u32 ph = 0;
+      int it = 0;
+      int u = u_begin, tile, k0, k1;
+      while (!*abort_flag && sk_next(u, u_end, nkb, tile, k0, k1)) {
+        const int acc = it & 1;
+        const u32 acc_ph = (it >> 1) & 1;
+        const u32 d_tmem = tmem_base + acc * Cfg::BN;
+        if (!mbar_wait(tempty_bar(acc), acc_ph ^ 1u, p.status, 0x23)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        for (int kb = k0; kb < k1; ++kb) {
+          if (!mbar_wait(full_bar(s), ph, p.status, 0x24)) {
+            *abort_flag = 1;
+            break;
+          }
+          tc_fence_after();
+          const u32 sa = stage0 + s * Cfg::STAGE_BYTES;
+          const u32 sb = sa + Cfg::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < Cfg::BK / Cfg::UMMA_K; ++k)
+            mma_f16_ss(d_tmem, operand_desc<Cfg>(sa, true, k), operand_desc<Cfg>(sb, false, k), Cfg::IDESC,
+                       (kb > k0 || k > 0) ? 1u : 0u);
+          tc_commit(empty_bar(s));
+          if (++s == Cfg::STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (*abort_flag) break;
+        tc_commit(tfull_bar(acc));
+        ++it;
+      }
+      tc_commit(drain_bar);
+      mbar_wait(drain_bar, 0, p.status, 0x25);
+    }
+    __syncwarp();
+  } else {
+    const int q = warp & 3;
+    const int row = q * 32 + lane;  // TMEM lane = output column (n) within the tile
+    unsigned short *out = static_cast<unsigned short *>(p.out);
+    int it = 0;
+    int u = u_begin, tile, k0, k1;
+    while (sk_next(u, u_end, nkb, tile, k0, k1)) {
+      const int acc = it & 1;
+      const u32 acc_ph = (it >> 1) & 1;
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait(tfull_bar(acc), acc_ph, p.status, 0x26);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      // one decision for all four warps: the partial path below has barriers
+      if (epi_vote_any(!ok || *abort_flag)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const u32 t_row = tmem_base + ((u32)(q * 32) << 16) + acc * Cfg::BN;
+      const int n = tile * Cfg::BM + row;
+      if (k0 == 0 && k1 == nkb) {
+        bf16_store_tile<Cfg>(p, t_row, n, 0);
+      } else {
+        const int first = sk_cta_of_unit(tile * nkb, sp.base, sp.extra);
+        const int nseg = sk_cta_of_unit((tile + 1) * nkb - 1, sp.base, sp.extra) - first + 1;
+        const int slot = blockIdx.x - first;
+        float *mine = sp.partial + ((static_cast<long long>(tile) * sp.max_seg + slot) * Cfg::BM + row) * Cfg::BN;
+        constexpr int CH = (Cfg::BN % 32 == 0) ? 32 : 16;
+#pragma unroll 1
+        for (int c0 = 0; c0 < Cfg::BN; c0 += CH) {
+          u32 r[CH];
+          if constexpr (CH == 32)
+            tmem_ld_32x32b_x32(t_row + c0, r);
+          else
+            tmem_ld_32x32b_x16(t_row + c0, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < CH / 4; ++j)
+            *reinterpret_cast<float4 *>(mine + c0 + 4 * j) =
+                make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                            __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+        }
+        __threadfence();
+        epi_bar();
+        if (threadIdx.x == 64) {
+          const unsigned old = atomicAdd(sp.counters + tile, 1u);
+          *last_flag = (old == static_cast<unsigned>(nseg - 1)) ? 1u : 0u;
+        }
+        epi_bar();
+        if (*last_flag) {
+          __threadfence();
+          // sum the slots in slot order; all loads of a slot are in flight at once
+          const float4 *slots = reinterpret_cast<const float4 *>(
+              sp.partial + (static_cast<long long>(tile) * sp.max_seg * Cfg::BM + row) * Cfg::BN);
+          constexpr int V = Cfg::BN / 4;
+          float4 sum[V];
+#pragma unroll
+          for (int j = 0; j < V; ++j) sum[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int sgi = 0; sgi < nseg; ++sgi) {
+            float4 v[V];
+#pragma unroll
+            for (int j = 0; j < V; ++j) v[j] = __ldcg(slots + static_cast<long long>(sgi) * Cfg::BM * V + j);
+#pragma unroll
+            for (int j = 0; j < V; ++j) {
+              sum[j].x += v[j].x;
+              sum[j].y += v[j].y;
+              sum[j].z += v[j].z;
+              sum[j].w += v[j].w;
+            }
+          }
+          if (n < p.out_cols) {
+            const float *f = reinterpret_cast<const float *>(sum);
+#pragma unroll
+            for (int m = 0; m < Cfg::BN; ++m)
+              if (m < p.out_rows)
+                st_global_b16(out + static_cast<long long>(m) * p.ldo + n, pack_bf16x2(f[m] * p.alpha, 0.0f));
+          }
+          if (threadIdx.x == 64) sp.counters[tile] = 0u;  // ready for the next launch
+        }
+        epi_bar();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar(acc));
+      ++it;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc<1>(tmem_base, Cfg::TMEM_COLS);
+}
+
+// ===========================================================================
 // 2-CTA variant: a cluster of two CTAs computes a 256 x BN tile with
 // tcgen05.mma.cta_group::2 (M = 256).  CTA rank r loads rows [128r, 128r+128)
 // of the A tile and columns [BN/2*r, BN/2*(r+1)) of the B tile into its own
@@ -379,6 +656,7 @@ template <class Cfg>
 __global__ void __launch_bounds__(192, 1)
     gemm2_kernel(const __grid_constant__ TensorMap tmap_a, const __grid_constant__ TensorMap tmap_b,
                  const Params p) {
+  pdl_launch_dependents();
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const u32 raw = smem_u32(smem_raw);
   const u32 base = (raw + 1023u) & ~1023u;
@@ -428,6 +706,7 @@ __global__ void __launch_bounds__(192, 1)
   cluster_sync();  // both CTAs' barriers are initialised before any remote use
   tc_fence_after();
   const u32 tmem_base = *tmem_slot;
+  pdl_wait();  // the previous kernel of the stream is complete from here on
 
   if (warp == 0) {
     // ------------------------------------------------ TMA producer (both CTAs)

@@ -112,6 +112,16 @@ __device__ __forceinline__ bool mbar_wait(u32 bar, u32 parity, u32 *status, u32 
   }
 }
 
+// ---------------------------------------------------------------- dependent launch
+// Allow the next kernel of the stream (launched with programmatic stream
+// serialisation) to start its prologue on SMs this grid frees.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// Wait until the preceding grid has completed and its writes are visible;
+// returns at once when the launch had no programmatic dependency.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ---------------------------------------------------------------- fences
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -8,6 +8,7 @@
 
 #include <cstdint>
 #include <mutex>
+#include <utility>
 
 #include "device/gemm_sm100.cuh"
 #include "thork_internal.h"
@@ -192,6 +193,36 @@ extern "C" int thork_matrix_add_f32(float *d_out, const float *d_a, const float 
 // ---------------------------------------------------------------------------
 // tcgen05 GEMMs
 // ---------------------------------------------------------------------------
+// Launch with programmatic stream serialisation (the kernel executes
+// griddepcontrol.wait before touching global memory) and an optional
+// cluster of `cluster_x` CTAs.
+template <class... KArgs, class... Args>
+static int launch_pdl(void (*kern)(KArgs...), dim3 grid, int threads, int smem, cudaStream_t s,
+                      int cluster_x, const char *name, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[n].val.programmaticStreamSerializationAllowed = 1;
+  ++n;
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (e != cudaSuccess) return thork_cuda_error(e, name);
+  return launch_check(name);
+}
+
 namespace {
 using namespace thork::gemm;
 
@@ -211,7 +242,7 @@ using CfgSkinny256 = Config<KIND_BF16, 256, 4, true, false, true>;
 
 enum KernelId {
   K_GEMM_BF16 = 0, K_GEMM_E4M3, K_SKINNY16, K_SKINNY32, K_SKINNY64, K_SKINNY128, K_SKINNY256,
-  K_GEMM2_BF16, K_GEMM2_E4M3
+  K_GEMM2_BF16, K_GEMM2_E4M3, K_SKSK16, K_SKSK32
 };
 
 template <class Cfg>
@@ -223,8 +254,7 @@ int run_gemm(int kernel_id, const TensorMap &ta, const TensorMap &tb, const Para
   if ((rc = thork_sm_count(&sms))) return rc;
   const int ntiles = ((prm.GM + Cfg::BM - 1) / Cfg::BM) * ((prm.GN + Cfg::BN - 1) / Cfg::BN);
   const int grid = ntiles < sms ? ntiles : sms;
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(ta, tb, prm);
-  return launch_check(name);
+  return launch_pdl(kern, dim3(grid), Cfg::THREADS, Cfg::SMEM_BYTES, s, 1, name, ta, tb, prm);
 }
 
 // Cluster-pair launch: grid = 2 x (pairs), cluster (2,1,1).
@@ -237,21 +267,7 @@ int run_gemm2(int kernel_id, const TensorMap &ta, const TensorMap &tb, const Par
   if ((rc = thork_sm_count(&sms))) return rc;
   const int ntiles = ((prm.GM + 2 * Cfg::BM - 1) / (2 * Cfg::BM)) * ((prm.GN + Cfg::BN - 1) / Cfg::BN);
   const int pairs = ntiles < sms / 2 ? ntiles : sms / 2;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * pairs, 1, 1);
-  cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
-  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, prm);
-  if (e != cudaSuccess) return thork_cuda_error(e, name);
-  return launch_check(name);
+  return launch_pdl(kern, dim3(2 * pairs), Cfg::THREADS, Cfg::SMEM_BYTES, s, 2, name, ta, tb, prm);
 }
 
 int check_dims(int M, int N, int K, int align, const char *what) {
@@ -325,6 +341,119 @@ extern "C" int thork_gemm_e4m3(const void *d_a, const void *d_b, void *d_c, int 
 }
 
 namespace {
+// ---- stream-K decode GEMM -------------------------------------------------
+struct SkPlan {
+  int grid, base, extra, tiles, max_seg;
+  size_t partial_bytes, counter_bytes;
+};
+
+int sk_cta_of_unit_host(int u, int base, int extra) {
+  const int big = extra * (base + 1);
+  return u < big ? u / (base + 1) : extra + (u - big) / base;
+}
+
+// Equal contiguous ranges of (tile, k-block) units over the SMs.
+SkPlan sk_plan(int M_pad_cols, int N, int K, int sms) {
+  SkPlan pl;
+  const int BM = 128, BK = 64;
+  pl.tiles = (N + BM - 1) / BM;
+  const int nkb = (K + BK - 1) / BK;
+  const long long units = static_cast<long long>(pl.tiles) * nkb;
+  pl.grid = static_cast<int>(units < sms ? units : sms);
+  pl.base = static_cast<int>(units / pl.grid);
+  pl.extra = static_cast<int>(units % pl.grid);
+  pl.max_seg = 1;
+  for (int t = 0; t < pl.tiles; ++t) {
+    const int c0 = sk_cta_of_unit_host(t * nkb, pl.base, pl.extra);
+    const int c1 = sk_cta_of_unit_host((t + 1) * nkb - 1, pl.base, pl.extra);
+    if (c1 - c0 + 1 > pl.max_seg) pl.max_seg = c1 - c0 + 1;
+  }
+  pl.partial_bytes = static_cast<size_t>(pl.tiles) * pl.max_seg * BM * M_pad_cols * sizeof(float);
+  pl.counter_bytes = static_cast<size_t>(pl.tiles) * sizeof(unsigned);
+  return pl;
+}
+
+// Per-device workspaces of the stream-K path: the partial slots, and the
+// per-tile arrival counters in a buffer of their own (zeroed when allocated
+// or grown; every launch returns the counters it uses to zero), so the
+// counters never land on memory an earlier plan used for partials.
+std::mutex g_ws_mu;
+void *g_part[kMaxDevices] = {};
+size_t g_part_bytes[kMaxDevices] = {};
+void *g_cnt[kMaxDevices] = {};
+size_t g_cnt_bytes[kMaxDevices] = {};
+
+int grow(void **buf, size_t *have, size_t need, bool zero, const char *what) {
+  if (*have >= need) return THORK_OK;
+  if (*buf) cudaFree(*buf);
+  *buf = nullptr;
+  *have = 0;
+  cudaError_t e = cudaMalloc(buf, need);
+  if (e != cudaSuccess) return thork_cuda_error(e, what);
+  if (zero) {
+    e = cudaMemset(*buf, 0, need);
+    if (e != cudaSuccess) return thork_cuda_error(e, what);
+  }
+  *have = need;
+  return THORK_OK;
+}
+
+int sk_workspace(size_t partial_bytes, size_t counter_bytes, void **partial, void **counters) {
+  int dev, rc;
+  if ((rc = current_device(&dev))) return rc;
+  std::lock_guard<std::mutex> lk(g_ws_mu);
+  if ((rc = grow(&g_part[dev], &g_part_bytes[dev], partial_bytes, false, "cudaMalloc(stream-K partials)")))
+    return rc;
+  if ((rc = grow(&g_cnt[dev], &g_cnt_bytes[dev], counter_bytes, true, "cudaMalloc(stream-K counters)")))
+    return rc;
+  *partial = g_part[dev];
+  *counters = g_cnt[dev];
+  return THORK_OK;
+}
+
+template <class Cfg>
+int launch_skinny_sk(int kernel_id, const TensorMap &ta, const TensorMap &tb, const Params &prm,
+                     const SkPlan &pl, void *partial, void *counters, cudaStream_t s) {
+  int rc;
+  auto kern = skinny_sk_kernel<Cfg>;
+  if ((rc = ensure_smem(reinterpret_cast<const void *>(kern), kernel_id, Cfg::SMEM_BYTES))) return rc;
+  SkParams sp;
+  sp.p = prm;
+  sp.partial = static_cast<float *>(partial);
+  sp.counters = static_cast<unsigned *>(counters);
+  sp.base = pl.base;
+  sp.extra = pl.extra;
+  sp.max_seg = pl.max_seg;
+  return launch_pdl(kern, dim3(pl.grid), Cfg::THREADS, Cfg::SMEM_BYTES, s, 1, "skinny_sk_kernel launch",
+                    ta, tb, sp);
+}
+
+template <class Cfg>
+int encode_skinny_maps(TensorMap &ta, TensorMap &tb, const void *d_x, const void *d_w, int M, int N,
+                       int K) {
+  int rc;
+  // A operand = W [K, N] (MN-major), B operand = X [M, K] (K-major, rows >= M read as zero)
+  if ((rc = thork_encode_tmap_2d(&ta, THORK_DT_BF16, d_w, K, N, (uint64_t)N * 2, Cfg::BK, Cfg::CHUNK, 128)))
+    return rc;
+  return thork_encode_tmap_2d(&tb, THORK_DT_BF16, d_x, M, K, (uint64_t)K * 2, Cfg::BN, Cfg::BK, 128);
+}
+
+template <class Cfg>
+int run_skinny_sk(int kernel_id, const void *d_x, const void *d_w, void *d_y, int M, int N, int K,
+                  cudaStream_t s) {
+  int rc, sms;
+  alignas(64) TensorMap ta, tb;
+  if ((rc = encode_skinny_maps<Cfg>(ta, tb, d_x, d_w, M, N, K))) return rc;
+  if ((rc = thork_sm_count(&sms))) return rc;
+  const SkPlan pl = sk_plan(Cfg::BN, N, K, sms);
+  void *part, *cnt;
+  if ((rc = sk_workspace(pl.partial_bytes, pl.counter_bytes, &part, &cnt))) return rc;
+  unsigned *status;
+  if ((rc = thork_status_word(&status))) return rc;
+  Params prm{d_y, N, M, K, N, M, N, 1.0f, status};
+  return launch_skinny_sk<Cfg>(kernel_id, ta, tb, prm, pl, part, cnt, s);
+}
+
 template <class Cfg>
 int run_skinny(int kernel_id, const void *d_x, const void *d_w, void *d_y, int M, int N, int K,
                cudaStream_t s) {
@@ -349,8 +478,10 @@ extern "C" int thork_skinny_gemm_bf16(const void *d_x, const void *d_w, void *d_
   if ((rc = check_dims(M, N, K, 8, "skinny_gemm_bf16"))) return rc;
   if ((rc = check_ptrs(d_x, d_w, d_y, "skinny_gemm_bf16"))) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (M <= 16) return run_skinny<CfgSkinny16>(K_SKINNY16, d_x, d_w, d_y, M, N, K, s);
-  if (M <= 32) return run_skinny<CfgSkinny32>(K_SKINNY32, d_x, d_w, d_y, M, N, K, s);
+  // M <= 32: stream-K over all SMs (partials are small); larger M: one CTA
+  // per 128-column tile
+  if (M <= 16) return run_skinny_sk<CfgSkinny16>(K_SKSK16, d_x, d_w, d_y, M, N, K, s);
+  if (M <= 32) return run_skinny_sk<CfgSkinny32>(K_SKSK32, d_x, d_w, d_y, M, N, K, s);
   if (M <= 64) return run_skinny<CfgSkinny64>(K_SKINNY64, d_x, d_w, d_y, M, N, K, s);
   if (M <= 128) return run_skinny<CfgSkinny128>(K_SKINNY128, d_x, d_w, d_y, M, N, K, s);
   if (M <= 256) return run_skinny<CfgSkinny256>(K_SKINNY256, d_x, d_w, d_y, M, N, K, s);
