@@ -211,6 +211,28 @@ THORK_API int thork_gemm_e4m3(const void *d_a, const void *d_b, void *d_c,
 THORK_API int thork_skinny_gemm_bf16(const void *d_x, const void *d_w, void *d_y,
                            int M, int N, int K, void *stream);
 
+/* Allocation-free form of thork_skinny_gemm_bf16 for 1 <= M <= 32 (the
+ * stream-K decode path).  No reference counterpart: it exists for callers
+ * that must not allocate device memory, directly or through this library --
+ * for example a serving process whose memory pool owns the whole GPU
+ * budget, or a latency-critical path that cannot afford the device-wide
+ * synchronisation cudaMalloc/cudaFree imply.  thork_skinny_gemm_bf16
+ * allocates its workspace (and status word) on first use; this entry point
+ * instead uses a fixed 8 MiB scratch array compiled into the library, which
+ * every GPU that loads the library holds until the process exits.
+ *   - The first call on a device looks up that device's address of the array;
+ *     make that first call before any stream capture.
+ *   - The scratch is shared by every call and keeps the last call's contents:
+ *     each call clears the parts that must start at zero, and calls that can
+ *     overlap on the GPU (different streams, other threads) race on it.
+ *   - Limits: M <= 32, ceil(N/128) <= 16384 output tiles, and the split-tile
+ *     partials of the problem must fit the array; larger requests return
+ *     THORK_ERR_INVALID with the sizes in the message.  Inputs, output and
+ *     stream are as for thork_skinny_gemm_bf16; no cudaMalloc, cudaFree or
+ *     other allocating call is made.                                       */
+THORK_API int thork_skinny_gemm_bf16_noalloc(const void *d_x, const void *d_w, void *d_y,
+                                            int M, int N, int K, void *stream);
+
 /* ---- NCCL (dlopen of libnccl.so.2; no reference counterpart) ---------- */
 /* Writes a 128-byte ncclUniqueId into id128.                              */
 THORK_API int thork_nccl_get_unique_id(void *id128);

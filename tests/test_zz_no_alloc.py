@@ -1,0 +1,60 @@
+"""The allocation-free decode GEMM entry point (thork_skinny_gemm_bf16_noalloc).
+
+It serves callers that must not allocate device memory themselves or
+through this library (a process whose memory pool owns the GPU, or a path
+that cannot take cudaMalloc's device-wide synchronisation).  Its scratch is
+a fixed array compiled into libthork_rt.so, shared by every call.  This test
+calls it through the C-ABI twice in a row and compares each result with the
+allocating entry point's output and with the oracle.  The file is collected
+last so that a run stopping at the first failure has run everything else."""
+
+import numpy as np
+import pytest
+
+import thork_b200 as tk
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+
+
+def test_no_alloc_entry_point_matches_allocating_one_twice():
+    rt = tk.runtime
+    lib = rt.lib()
+    rt.get_device()
+    m, n, k = 16, 14336, 4096
+    x, w = oracle.skinny_inputs(m, n, k, seed=12)
+    x16, w16 = oracle.f32_to_bf16_bits(x), oracle.f32_to_bf16_bits(w)
+    dx, dw = rt.to_device(x16), rt.to_device(w16)
+
+    y_ref = rt.empty((m, n), np.uint16)
+    rt.check(lib.thork_skinny_gemm_bf16(dx.ptr, dw.ptr, y_ref.ptr, m, n, k, None))
+    rt.synchronize()
+    ref = oracle.bf16_bits_to_f32(y_ref.to_host())
+    exact = oracle.gemm_bf16_ref(x16, w16)
+
+    for call in range(2):
+        y = rt.empty((m, n), np.uint16)
+        y.zero()
+        rt.check(lib.thork_skinny_gemm_bf16_noalloc(dx.ptr, dw.ptr, y.ptr, m, n, k, None))
+        rt.synchronize()
+        got = oracle.bf16_bits_to_f32(y.to_host())
+        err = oracle.max_rel_err(got, ref)
+        assert err <= TOL, f"call {call}: max rel err vs allocating entry point {err:.3e}"
+        assert oracle.max_rel_err(got, exact) <= TOL
+    assert rt.kernel_status() == 0
+
+
+def test_no_alloc_entry_point_rejects_oversized_requests():
+    rt = tk.runtime
+    lib = rt.lib()
+    rt.get_device()
+    dummy = rt.empty((1024,), np.uint16)
+    assert lib.thork_skinny_gemm_bf16_noalloc(dummy.ptr, dummy.ptr, dummy.ptr, 33, 1024, 512, None) \
+        == rt.ERR_INVALID
+    assert "M must be <= 32" in rt.last_error()
+    # 32 rows x 1M columns x 8192 deep: split-tile partials exceed the array
+    assert lib.thork_skinny_gemm_bf16_noalloc(dummy.ptr, dummy.ptr, dummy.ptr, 32, 1 << 20, 8192, None) \
+        == rt.ERR_INVALID
+    assert "scratch array" in rt.last_error()

@@ -487,3 +487,83 @@ extern "C" int thork_skinny_gemm_bf16(const void *d_x, const void *d_w, void *d_
   if (M <= 256) return run_skinny<CfgSkinny256>(K_SKINNY256, d_x, d_w, d_y, M, N, K, s);
   return thork_set_error(THORK_ERR_INVALID, "skinny_gemm_bf16: M must be <= 256 (M=%d)", M);
 }
+
+// ---------------------------------------------------------------------------
+// allocation-free decode GEMM (thork_skinny_gemm_bf16_noalloc)
+// ---------------------------------------------------------------------------
+// Scratch layout: [status word, 256 B][tile counters, 64 KiB][partial slots].
+// The array is zero when the library's module loads; each call clears the
+// status word and the counters it will use before launching.
+namespace {
+constexpr size_t kNoAllocBytes = 8u << 20;
+constexpr size_t kNoAllocStatusBytes = 256;
+constexpr size_t kNoAllocCounterBytes = 64u << 10;
+constexpr size_t kNoAllocPartialBytes = kNoAllocBytes - kNoAllocStatusBytes - kNoAllocCounterBytes;
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+namespace {
+std::mutex g_na_mu;
+unsigned char *g_na_addr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device (looked up once
+// per device; the host-side name is only a stand-in for it).
+int noalloc_scratch(unsigned char **addr) {
+  int dev, rc;
+  if ((rc = current_device(&dev))) return rc;
+  std::lock_guard<std::mutex> lk(g_na_mu);
+  if (!g_na_addr[dev]) {
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return thork_cuda_error(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    g_na_addr[dev] = static_cast<unsigned char *>(p);
+  }
+  *addr = g_na_addr[dev];
+  return THORK_OK;
+}
+
+template <class Cfg>
+int run_skinny_noalloc(int kernel_id, const void *d_x, const void *d_w, void *d_y, int M, int N, int K,
+                       cudaStream_t s) {
+  int rc, sms;
+  if ((rc = thork_sm_count(&sms))) return rc;
+  const SkPlan pl = sk_plan(Cfg::BN, N, K, sms);
+  if (pl.partial_bytes > kNoAllocPartialBytes)
+    return thork_set_error(THORK_ERR_INVALID,
+                           "skinny_gemm_bf16_noalloc: M=%d N=%d K=%d needs %zu bytes of split-tile "
+                           "partials; the scratch array holds %zu",
+                           M, N, K, pl.partial_bytes, kNoAllocPartialBytes);
+  unsigned char *base;
+  if ((rc = noalloc_scratch(&base))) return rc;
+  unsigned char *counters = base + kNoAllocStatusBytes;
+  unsigned char *partial = counters + kNoAllocCounterBytes;
+  // the status word and this plan's tile counters must start at zero
+  cudaError_t e = cudaMemsetAsync(base, 0, kNoAllocStatusBytes + pl.counter_bytes, s);
+  if (e != cudaSuccess) return thork_cuda_error(e, "cudaMemsetAsync(no-alloc scratch)");
+  alignas(64) TensorMap ta, tb;
+  if ((rc = encode_skinny_maps<Cfg>(ta, tb, d_x, d_w, M, N, K))) return rc;
+  Params prm{d_y, N, M, K, N, M, N, 1.0f, reinterpret_cast<unsigned *>(base)};
+  return launch_skinny_sk<Cfg>(kernel_id, ta, tb, prm, pl, partial, counters, s);
+}
+}  // namespace
+
+extern "C" int thork_skinny_gemm_bf16_noalloc(const void *d_x, const void *d_w, void *d_y, int M,
+                                              int N, int K, void *stream) {
+  int rc;
+  if ((rc = check_dims(M, N, K, 8, "skinny_gemm_bf16_noalloc"))) return rc;
+  if (M > 32)
+    return thork_set_error(THORK_ERR_INVALID,
+                           "skinny_gemm_bf16_noalloc: M must be <= 32 (M=%d); use "
+                           "thork_skinny_gemm_bf16 for larger M",
+                           M);
+  if (static_cast<size_t>((N + 127) / 128) * sizeof(unsigned) > kNoAllocCounterBytes)
+    return thork_set_error(THORK_ERR_INVALID,
+                           "skinny_gemm_bf16_noalloc: N=%d gives %d output tiles; at most %zu fit the "
+                           "scratch array",
+                           N, (N + 127) / 128, kNoAllocCounterBytes / sizeof(unsigned));
+  if ((rc = check_ptrs(d_x, d_w, d_y, "skinny_gemm_bf16_noalloc"))) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (M <= 16) return run_skinny_noalloc<CfgSkinny16>(K_SKSK16, d_x, d_w, d_y, M, N, K, s);
+  return run_skinny_noalloc<CfgSkinny32>(K_SKSK32, d_x, d_w, d_y, M, N, K, s);
+}

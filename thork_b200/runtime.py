@@ -90,6 +90,7 @@ _SIGNATURES = {
     "thork_gemm_bf16": [_vp, _vp, _vp, _i, _i, _i, _i, _vp],
     "thork_gemm_e4m3": [_vp, _vp, _vp, _i, _i, _i, ctypes.c_float, ctypes.c_float, _i, _vp],
     "thork_skinny_gemm_bf16": [_vp, _vp, _vp, _i, _i, _i, _vp],
+    "thork_skinny_gemm_bf16_noalloc": [_vp, _vp, _vp, _i, _i, _i, _vp],
     "thork_nccl_get_unique_id": [_vp],
     "thork_nccl_comm_init_rank": [_pvp, _i, _vp, _i],
     "thork_nccl_comm_destroy": [_vp],
