@@ -164,9 +164,10 @@ def bf16_bits(x):
 
 
 class GemmWorkload:
-    """bf16 / e4m3 GEMM, rows of A split over ranks, C all-gathered."""
+    """bf16 / e4m3 GEMM, rows of A split over ranks, C all-gathered (fused
+    into the GEMM epilogue over NVLink peer memory, or by NCCL)."""
 
-    def __init__(self, size: int, kind: str, d: Dist, rt, dist_mod):
+    def __init__(self, size: int, kind: str, d: Dist, rt, dist_mod, gather: str = "fused"):
         self.m = self.n = self.k = size
         self.kind = kind
         self.d = d
@@ -193,9 +194,10 @@ class GemmWorkload:
         self.elem = self.a_host.dtype.itemsize
         self.A = rt.DeviceArray.from_host(self.a_host)
         self.B = rt.DeviceArray.from_host(self.b_host)
+        self.gather = gather if d.world > 1 else "none"
         rows_out = self.m if d.world > 1 else self.m_loc
-        self.C = rt.empty((rows_out, self.n), np.uint16)
-        self.comm = None
+        self.C = rt.empty((rows_out, self.n), np.uint16) if self.gather != "fused" else None
+        self.comm = self.fg = None
         if d.world > 1:
             uid = None
             if d.rank == 0:
@@ -205,6 +207,10 @@ class GemmWorkload:
                 uid = bytes(buf)
             uid = d.bcast_bytes(uid)
             self.comm = dist_mod.Communicator(d.rank, d.world, unique_id=uid)
+            if self.gather == "fused":
+                self.fg = dist_mod.FusedGather(self.comm, self.m, self.n)
+        # our kernels per step: the GEMM, plus the flag barrier when fused
+        self.launches_per_step = 2 if self.gather == "fused" else 1
 
     flops_total = property(lambda self: 2.0 * self.m * self.n * self.k)
     flops_local = property(lambda self: 2.0 * self.m_loc * self.n * self.k)
@@ -212,6 +218,10 @@ class GemmWorkload:
     def step(self, stream, ev0=None, ev1=None):
         if ev0 is not None:
             ev0.record(stream)
+        if self.fg is not None:
+            self.fg.matmul(self.A, self.B, stream, gemm_done=ev1, dtype=self.kind,
+                           scale_a=self.scale)
+            return
         self.dist.sharded_matmul(self.comm, self.A, self.B, self.C, self.m, dtype=self.kind,
                                  scale=self.scale, gather=self.d.world > 1, stream=stream,
                                  gemm_done=ev1)
@@ -237,7 +247,7 @@ class GemmWorkload:
                 mm(self.pc, self.pa, self.pb, self.scale, 1.0)
             return
         self.dist.sharded_matmul_host(self.comm, self.pa, self.pb, self.pc, self.m,
-                                      dtype=self.kind, scale=self.scale)
+                                      dtype=self.kind, scale=self.scale, fused=self.fg)
 
     def cpu_sample(self, seconds: float):
         """The reference's check (NumPy fp32 matmul of the rounded inputs) on a
@@ -382,13 +392,13 @@ class AddWorkload:
         return 12.0 * n * reps / dt_s / 1e9, f"{reps} x NumPy a+b over {n} fp32", None
 
 
-def make_workload(name, d, rt, dist_mod):
+def make_workload(name, d, rt, dist_mod, gather="fused"):
     if name == "bf16_gemm_8192":
-        return GemmWorkload(8192, "bf16", d, rt, dist_mod)
+        return GemmWorkload(8192, "bf16", d, rt, dist_mod, gather)
     if name == "bf16_gemm_4096":
-        return GemmWorkload(4096, "bf16", d, rt, dist_mod)
+        return GemmWorkload(4096, "bf16", d, rt, dist_mod, gather)
     if name == "e4m3_gemm_8192":
-        return GemmWorkload(8192, "e4m3", d, rt, dist_mod)
+        return GemmWorkload(8192, "e4m3", d, rt, dist_mod, gather)
     if name.startswith("skinny_m"):
         return SkinnyWorkload(int(name[len("skinny_m"):]), d, rt, dist_mod)
     if name == "add_f32":
@@ -402,7 +412,9 @@ def describe(name, w, world):
             "workload": name, "M": w.m, "N": w.n, "K": w.k,
             "dtype_in": w.kind, "dtype_out": "bf16", "accumulate": "fp32",
             "parallelism": (f"A rows split over {world} GPUs, B replicated, C all-gathered "
-                            "with NCCL" if world > 1 else "1 GPU"),
+                            + ("inside the GEMM epilogue (P2P stores over NVLink + device flag "
+                               "barrier)" if w.gather == "fused" else "with NCCL")
+                            if world > 1 else "1 GPU"),
             "l2_policy": "inputs+output larger than L2 (no flush needed)",
         }, "TFLOP/s", "tensor"
     if isinstance(w, SkinnyWorkload):
@@ -449,7 +461,7 @@ def run_thork(args, d: Dist):
     rt = tk.runtime
     rt.set_device(d.local_rank)
     peaks, peak_src = load_peaks()
-    w = make_workload(args.workload, d, rt, dist_mod)
+    w = make_workload(args.workload, d, rt, dist_mod, args.gather)
     cfg, unit, bound = describe(args.workload, w, d.world)
 
     sampler = ClockSampler(d.local_rank)
@@ -508,7 +520,7 @@ def run_thork(args, d: Dist):
         "e2e": {"value": round(e2e_val, 3), "unit": unit, "h2d_bytes_per_step": int(w.h2d),
                 "d2h_bytes_per_step": int(w.d2h), "steps": e2e_steps,
                 "api": "tk.kernels.matmul/matrix_add" if d.world == 1 else "thork_b200.dist.sharded_matmul_host"},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * getattr(w, "launches_per_step", 1),
         "clocks": clocks,
     }
     if d.rank == 0 and d.world == 1:
@@ -522,6 +534,8 @@ def run_thork(args, d: Dist):
     if traffic is not None:
         line["roofline"]["traffic"] = traffic
     if w.__class__ is GemmWorkload and w.comm is not None:
+        if w.fg is not None:
+            w.fg.close()
         w.comm.close()
     if d.rank == 0:
         print(json.dumps(line), flush=True)
@@ -646,6 +660,8 @@ def main():
     ap.add_argument("--workload", default="bf16_gemm_8192")
     ap.add_argument("--impl", default="thork", choices=["thork", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--gather", default="fused", choices=["fused", "nccl"],
+                    help="multi-GPU GEMM: all-gather fused into the epilogue, or NCCL after it")
     ap.add_argument("--no-also", dest="also", action="store_false",
                     help="omit the short timings of the other configs")
     args = ap.parse_args()

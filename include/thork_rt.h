@@ -69,7 +69,10 @@ enum {
   THORK_ATTR_SMEM_OPTIN = 3,      /* max dynamic smem per block (opt-in)   */
   THORK_ATTR_L2_BYTES = 4,
   THORK_ATTR_CLOCK_KHZ = 5,
-  THORK_ATTR_MEM_CLOCK_KHZ = 6
+  THORK_ATTR_MEM_CLOCK_KHZ = 6,
+  THORK_ATTR_PCI_DOMAIN = 7,      /* PCI location: identifies the physical GPU */
+  THORK_ATTR_PCI_BUS = 8,
+  THORK_ATTR_PCI_DEVICE = 9
 };
 
 /* ---- library / errors ----------------------------------------------- */
@@ -210,6 +213,39 @@ THORK_API int thork_gemm_e4m3(const void *d_a, const void *d_b, void *d_c,
  * (src/thork/kernels/matmul.py:17-71).                                     */
 THORK_API int thork_skinny_gemm_bf16(const void *d_x, const void *d_w, void *d_y,
                            int M, int N, int K, void *stream);
+
+/* C[M,N] rows [row0, row0+rows) = A_rows . B, written both to d_c (this
+ * GPU's full M x N result buffer) and, over NVLink, to the same rows of each
+ * peer's result buffer d_peer_c[0..n_peers) (pointers opened with
+ * thork_ipc_open).  This fuses the GEMM with the all-gather of C: after all
+ * ranks' launches complete (e.g. behind an NCCL all-reduce used as a
+ * barrier), every rank holds the full C.  bf16 in/out, same constraints and
+ * variants as thork_gemm_bf16, at most 7 peers.  No reference counterpart
+ * (the reference is single-GPU, src/thork/runtime.py:85-105).             */
+THORK_API int thork_gemm_bf16_allgather(const void *d_a_rows, const void *d_b, void *d_c,
+                                        void *const *d_peer_c, int n_peers, int rows, int N, int K,
+                                        int row0, int variant, void *stream);
+/* FP8 form of thork_gemm_bf16_allgather: e4m3 A rows and B (K, N multiples
+ * of 16), C = scale_a * scale_b * A.B in bf16 rows on this GPU and every
+ * peer.  No reference counterpart.                                         */
+THORK_API int thork_gemm_e4m3_allgather(const void *d_a_rows, const void *d_b, void *d_c,
+                                        void *const *d_peer_c, int n_peers, int rows, int N, int K,
+                                        int row0, float scale_a, float scale_b, int variant,
+                                        void *stream);
+/* Device-side barrier of the fused all-gather: this rank stores `epoch` into
+ * slot `rank` of every peer's flag array (d_peer_flags[q], q != rank, each
+ * `world` unsigned words in the peer's memory opened with thork_ipc_open)
+ * after a system-scope fence, then waits until its own d_flags[q] reach
+ * `epoch` for all q != rank.  The wait is bounded (1 s); on expiry the
+ * kernel status word records it and the barrier returns.  One rank per GPU,
+ * world <= 8.  No reference counterpart.                                   */
+THORK_API int thork_peer_barrier(void *d_flags, void *const *d_peer_flags, int world, int rank,
+                                 unsigned epoch, void *stream);
+/* CUDA IPC for the fused all-gather: export a cudaMalloc'd buffer (64-byte
+ * handle), open a peer's handle in this process, close it.                 */
+THORK_API int thork_ipc_handle(const void *d_ptr, void *handle64);
+THORK_API int thork_ipc_open(const void *handle64, void **d_ptr);
+THORK_API int thork_ipc_close(void *d_ptr);
 
 /* Allocation-free form of thork_skinny_gemm_bf16 for 1 <= M <= 32 (the
  * stream-K decode path).  No reference counterpart: it exists for callers

@@ -59,6 +59,23 @@ def test_library_kernels_reject_bad_shapes_before_touching_a_device():
     assert L.thork_matrix_add_f32(None, None, None, 0, None) == 0  # empty is a no-op
 
 
+def test_fused_allgather_and_barrier_reject_bad_arguments_on_the_host():
+    L = rt.lib()
+    peers = (ctypes.c_void_p * 7)(*([32] * 7))
+    assert L.thork_gemm_bf16_allgather(16, 16, 16, peers, 8, 64, 64, 64, 0, 0, None) == rt.ERR_INVALID
+    assert "n_peers" in rt.last_error()
+    assert L.thork_gemm_bf16_allgather(16, 16, 16, peers, 1, 64, 64, 64, 0, 2, None) == rt.ERR_INVALID
+    assert "variant" in rt.last_error()
+    bad = (ctypes.c_void_p * 7)(*([40] * 7))  # not 16-byte aligned
+    assert L.thork_gemm_bf16_allgather(16, 16, 16, bad, 1, 64, 64, 64, 0, 0, None) == rt.ERR_INVALID
+    assert L.thork_gemm_bf16_allgather(16, 16, 16, peers, 1, 64, 64, 64, -1, 0, None) == rt.ERR_INVALID
+    flags = (ctypes.c_void_p * 8)()
+    assert L.thork_peer_barrier(16, flags, 9, 0, 1, None) == rt.ERR_INVALID
+    assert L.thork_peer_barrier(16, flags, 2, 2, 1, None) == rt.ERR_INVALID
+    assert L.thork_peer_barrier(16, flags, 2, 0, 1, None) == rt.ERR_INVALID  # peer flags NULL
+    assert L.thork_ipc_handle(None, None) == rt.ERR_INVALID
+
+
 def test_nccl_fault_injection_is_host_side(monkeypatch):
     monkeypatch.setenv("THORK_FAULT_NCCL_INIT", "1")
     comm = ctypes.c_void_p()

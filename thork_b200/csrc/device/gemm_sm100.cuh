@@ -54,6 +54,12 @@ struct Config {
   // stages + barriers (full/empty per stage, tmem full/empty x2, teardown) + tmem slot
   static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+  // fused all-gather epilogue: each epilogue warp stages 32 rows x EPI_COLS
+  // bf16 in shared memory so that its global stores are whole 128-byte lines
+  static constexpr int EPI_COLS = 64;
+  static constexpr int EPI_OFF = STAGES * STAGE_BYTES + ((BAR_BYTES + 127) & ~127);
+  static constexpr int EPI_WARP_BYTES = 32 * EPI_COLS * 2;
+  static constexpr int SMEM_BYTES_PEERS = 1024 + EPI_OFF + 4 * EPI_WARP_BYTES;
   static constexpr u32 IDESC =
       make_idesc(KIND == KIND_BF16 ? 1u : 0u, KIND == KIND_BF16 ? 1u : 0u, A_MN, B_MN, BM, BN);
 
@@ -63,6 +69,11 @@ struct Config {
   static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
 };
 
+template <class Cfg, bool PEERS>
+constexpr int smem_bytes() {
+  return PEERS ? Cfg::SMEM_BYTES_PEERS : Cfg::SMEM_BYTES;
+}
+
 struct Params {
   void *out;      // bf16 output
   int GM, GN, GK; // MMA-space extents
@@ -71,6 +82,10 @@ struct Params {
   int out_cols;   // cols of the output matrix
   float alpha;
   u32 *status;
+  // fused all-gather: the same output rows are also stored at the same
+  // offsets of up to 7 peer GPUs' buffers (P2P stores over NVLink)
+  void *peer[7];
+  int npeer;
 };
 
 // Output-tile order: groups of GROUP_M tile-rows walked column by column, so
@@ -156,7 +171,62 @@ __device__ __forceinline__ void bf16_store_tile(const Params &p, u32 t_row, int 
   }
 }
 
+// Epilogue of the fused all-gather for one warp's 32 accumulator rows
+// (TMEM lanes of t_row, output rows row0..row0+31, columns col0..col0+BN):
+// each EPI_COLS-wide slice goes TMEM -> registers -> bf16 -> this warp's
+// staging buffer (row = lane, 16-byte chunks XOR-swizzled by row so both
+// directions are bank-conflict free), then back out with lanes covering
+// consecutive 16-byte chunks of a row: every warp store writes whole
+// 128-byte lines, to this GPU's C and to each peer's C at the same offset.
 template <class Cfg>
+__device__ __forceinline__ void bf16_store_tile_peers(const Params &p, u32 t_row, int row0,
+                                                      int col0, unsigned char *stg, int lane) {
+  constexpr int EC = Cfg::EPI_COLS;
+  constexpr int RB = EC * 2;     // staged bytes per row
+  constexpr int CPR = RB / 16;   // 16-byte chunks per row
+  constexpr int RPI = 32 / CPR;  // rows per warp store instruction
+  static_assert(CPR == 8 && Cfg::BN % EC == 0, "staging assumes 128-byte rows");
+  unsigned short *out = static_cast<unsigned short *>(p.out);
+#pragma unroll 1
+  for (int c0 = 0; c0 < Cfg::BN; c0 += EC) {
+#pragma unroll
+    for (int h = 0; h < EC; h += 32) {
+      u32 r[32];
+      tmem_ld_32x32b_x32(t_row + c0 + h, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        u32 w[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          w[q] = pack_bf16x2(__uint_as_float(r[8 * j + 2 * q]) * p.alpha,
+                             __uint_as_float(r[8 * j + 2 * q + 1]) * p.alpha);
+        const int chunk = h / 8 + j;
+        *reinterpret_cast<uint4 *>(stg + lane * RB + ((chunk ^ (lane & (CPR - 1))) * 16)) =
+            make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+    __syncwarp();
+#pragma unroll 2
+    for (int it = 0; it < 32 / RPI; ++it) {
+      const int r = it * RPI + lane / CPR;
+      const int chunk = lane % CPR;
+      const uint4 v = *reinterpret_cast<const uint4 *>(stg + r * RB + ((chunk ^ (r & (CPR - 1))) * 16));
+      const int row = row0 + r, col = col0 + c0 + chunk * 8;
+      if (row < p.out_rows && col < p.out_cols) {
+        const long long off = static_cast<long long>(row) * p.ldo + col;
+        st_global_v4(out + off, v.x, v.y, v.z, v.w);
+#pragma unroll
+        for (int g = 0; g < 7; ++g)  // constant indices keep p.peer in parameter space
+          if (g < p.npeer)
+            st_global_v4(static_cast<unsigned short *>(p.peer[g]) + off, v.x, v.y, v.z, v.w);
+      }
+    }
+    __syncwarp();
+  }
+}
+
+template <class Cfg, bool PEERS = false>
 __global__ void __launch_bounds__(192, 1)
     gemm_kernel(const __grid_constant__ TensorMap tmap_a, const __grid_constant__ TensorMap tmap_b,
                 const Params p) {
@@ -318,11 +388,18 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const int row_mma = tm * Cfg::BM + q * 32 + lane;  // MMA-space row owned by this thread
       const u32 t_row = tmem_base + ((u32)(q * 32) << 16) + acc * Cfg::BN;
-      bf16_store_tile<Cfg>(p, t_row, row_mma, tn * Cfg::BN);
+      if constexpr (PEERS)
+        bf16_store_tile_peers<Cfg>(p, t_row, tm * Cfg::BM + q * 32, tn * Cfg::BN,
+                                   smem + Cfg::EPI_OFF + q * Cfg::EPI_WARP_BYTES, lane);
+      else
+        bf16_store_tile<Cfg>(p, t_row, row_mma, tn * Cfg::BN);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(acc));
     }
+    // peer stores are ordered before anything a later kernel signals to
+    // the peers (the fused all-gather's flag barrier)
+    if constexpr (PEERS) __threadfence_system();
   }
 
   tc_fence_before();
@@ -634,6 +711,12 @@ struct Config2 {
   static constexpr int THREADS = 192;
   static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+  // fused all-gather epilogue: each epilogue warp stages 32 rows x EPI_COLS
+  // bf16 in shared memory so that its global stores are whole 128-byte lines
+  static constexpr int EPI_COLS = 64;
+  static constexpr int EPI_OFF = STAGES * STAGE_BYTES + ((BAR_BYTES + 127) & ~127);
+  static constexpr int EPI_WARP_BYTES = 32 * EPI_COLS * 2;
+  static constexpr int SMEM_BYTES_PEERS = 1024 + EPI_OFF + 4 * EPI_WARP_BYTES;
   static constexpr u32 IDESC =
       make_idesc(KIND == KIND_BF16 ? 1u : 0u, KIND == KIND_BF16 ? 1u : 0u, false, true, 256, BN);
   static_assert(BN % 32 == 0 && BN <= 256, "pair tile N must be a multiple of 32, at most 256");

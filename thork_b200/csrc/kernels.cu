@@ -242,19 +242,21 @@ using CfgSkinny256 = Config<KIND_BF16, 256, 4, true, false, true>;
 
 enum KernelId {
   K_GEMM_BF16 = 0, K_GEMM_E4M3, K_SKINNY16, K_SKINNY32, K_SKINNY64, K_SKINNY128, K_SKINNY256,
-  K_GEMM2_BF16, K_GEMM2_E4M3, K_SKSK16, K_SKSK32
+  K_GEMM2_BF16, K_GEMM2_E4M3, K_SKSK16, K_SKSK32, K_GEMM_BF16_AG, K_GEMM_E4M3_AG
 };
 
-template <class Cfg>
+template <class Cfg, bool PEERS = false>
 int run_gemm(int kernel_id, const TensorMap &ta, const TensorMap &tb, const Params &prm,
              cudaStream_t s, const char *name) {
   int rc, sms;
-  auto kern = gemm_kernel<Cfg>;
-  if ((rc = ensure_smem(reinterpret_cast<const void *>(kern), kernel_id, Cfg::SMEM_BYTES))) return rc;
+  auto kern = gemm_kernel<Cfg, PEERS>;
+  constexpr int smem = smem_bytes<Cfg, PEERS>();
+  static_assert(smem <= 232448, "shared memory budget exceeded");
+  if ((rc = ensure_smem(reinterpret_cast<const void *>(kern), kernel_id, smem))) return rc;
   if ((rc = thork_sm_count(&sms))) return rc;
   const int ntiles = ((prm.GM + Cfg::BM - 1) / Cfg::BM) * ((prm.GN + Cfg::BN - 1) / Cfg::BN);
   const int grid = ntiles < sms ? ntiles : sms;
-  return launch_pdl(kern, dim3(grid), Cfg::THREADS, Cfg::SMEM_BYTES, s, 1, name, ta, tb, prm);
+  return launch_pdl(kern, dim3(grid), Cfg::THREADS, smem, s, 1, name, ta, tb, prm);
 }
 
 // Cluster-pair launch: grid = 2 x (pairs), cluster (2,1,1).
@@ -338,6 +340,120 @@ extern "C" int thork_gemm_e4m3(const void *d_a, const void *d_b, void *d_c, int 
   if (variant == 0) variant = (M > 128) ? 2 : 1;
   if (variant == 2) return run_gemm2<Cfg2E4m3>(K_GEMM2_E4M3, ta, tb, prm, s, "gemm2_e4m3 launch");
   return run_gemm<C>(K_GEMM_E4M3, ta, tb, prm, s, "gemm_e4m3 launch");
+}
+
+// ---------------------------------------------------------------------------
+// Fused GEMM + all-gather over NVLink peer memory
+// ---------------------------------------------------------------------------
+namespace {
+// Shared body of the fused GEMM + all-gather entry points: this rank's rows
+// [row0, row0 + rows) of C go to d_c and to every peer buffer at the same
+// offset (1-CTA kernel with the peer-store epilogue).
+template <class Cfg>
+int gemm_allgather(int kernel_id, int dt, int elem, const void *d_a_rows, const void *d_b,
+                   void *d_c, void *const *d_peer_c, int n_peers, int rows, int N, int K, int row0,
+                   float alpha, int variant, void *stream, const char *what) {
+  int rc;
+  if ((rc = check_dims(rows, N, K, 16 / elem, what))) return rc;
+  if ((rc = check_ptrs(d_a_rows, d_b, d_c, what))) return rc;
+  if (variant < 0 || variant > 1)
+    return thork_set_error(THORK_ERR_INVALID, "%s: variant %d not supported (0 or 1)", what,
+                           variant);
+  if (n_peers < 0 || n_peers > 7 || (n_peers > 0 && !d_peer_c))
+    return thork_set_error(THORK_ERR_INVALID, "%s: n_peers=%d must be 0..7", what, n_peers);
+  if (row0 < 0) return thork_set_error(THORK_ERR_INVALID, "%s: row0 < 0", what);
+  for (int g = 0; g < n_peers; ++g)
+    if (!d_peer_c[g] || (reinterpret_cast<uintptr_t>(d_peer_c[g]) & 15u))
+      return thork_set_error(THORK_ERR_INVALID,
+                             "%s: peer buffer %d is NULL or not 16-byte aligned", what, g);
+  alignas(64) TensorMap ta, tb;
+  if ((rc = thork_encode_tmap_2d(&ta, dt, d_a_rows, rows, K, (uint64_t)K * elem, Cfg::BM, Cfg::BK,
+                                 128)))
+    return rc;
+  if ((rc = thork_encode_tmap_2d(&tb, dt, d_b, K, N, (uint64_t)N * elem, Cfg::BK, Cfg::CHUNK, 128)))
+    return rc;
+  unsigned *status;
+  if ((rc = thork_status_word(&status))) return rc;
+  const size_t off = static_cast<size_t>(row0) * N * 2;  // bytes to this rank's bf16 rows
+  Params prm{static_cast<char *>(d_c) + off, rows, N, K, N, rows, N, alpha, status};
+  for (int g = 0; g < n_peers; ++g) prm.peer[g] = static_cast<char *>(d_peer_c[g]) + off;
+  prm.npeer = n_peers;
+  return run_gemm<Cfg, true>(kernel_id, ta, tb, prm, static_cast<cudaStream_t>(stream), what);
+}
+}  // namespace
+
+extern "C" int thork_gemm_bf16_allgather(const void *d_a_rows, const void *d_b, void *d_c,
+                                        void *const *d_peer_c, int n_peers, int rows, int N, int K,
+                                        int row0, int variant, void *stream) {
+  return gemm_allgather<CfgBf16>(K_GEMM_BF16_AG, THORK_DT_BF16, 2, d_a_rows, d_b, d_c, d_peer_c,
+                                 n_peers, rows, N, K, row0, 1.0f, variant, stream,
+                                 "gemm_bf16_allgather");
+}
+
+extern "C" int thork_gemm_e4m3_allgather(const void *d_a_rows, const void *d_b, void *d_c,
+                                        void *const *d_peer_c, int n_peers, int rows, int N, int K,
+                                        int row0, float scale_a, float scale_b, int variant,
+                                        void *stream) {
+  return gemm_allgather<CfgE4m3>(K_GEMM_E4M3_AG, THORK_DT_E4M3, 1, d_a_rows, d_b, d_c, d_peer_c,
+                                 n_peers, rows, N, K, row0, scale_a * scale_b, variant, stream,
+                                 "gemm_e4m3_allgather");
+}
+
+namespace {
+// Flag barrier between the ranks of a fused all-gather.  Rank r stores
+// `epoch` into flags[r] of every peer (release at system scope, after a
+// system fence that orders this GPU's earlier peer stores), then waits, at
+// most THORK_WAIT_TIMEOUT_NS, until its own flags[q] reach `epoch` for every
+// peer q (acquire).  Flags compare by wrapping difference.
+struct PeerFlagPtrs {
+  unsigned *p[8];
+};
+
+__global__ void peer_barrier_kernel(const PeerFlagPtrs peers, unsigned *flags, int world, int rank,
+                                    unsigned epoch, unsigned *status) {
+  const int t = threadIdx.x;
+  if (t < world && t != rank) {
+    __threadfence_system();
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(peers.p[t] + rank), "r"(epoch)
+                 : "memory");
+    const uint64_t t0 = thork::dev::globaltimer();
+    for (;;) {
+      unsigned v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + t) : "memory");
+      if (static_cast<int>(v - epoch) >= 0) break;
+      if (thork::dev::globaltimer() - t0 > THORK_WAIT_TIMEOUT_NS) {
+        thork::dev::report_status(status, thork::dev::STATUS_WAIT_TIMEOUT, 20);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+}
+}  // namespace
+
+extern "C" int thork_peer_barrier(void *d_flags, void *const *d_peer_flags, int world, int rank,
+                                  unsigned epoch, void *stream) {
+  if (world < 1 || world > 8 || rank < 0 || rank >= world)
+    return thork_set_error(THORK_ERR_INVALID, "peer_barrier: rank %d / world %d (at most 8)", rank,
+                           world);
+  if (!d_flags || (world > 1 && !d_peer_flags))
+    return thork_set_error(THORK_ERR_INVALID, "peer_barrier: NULL flags");
+  PeerFlagPtrs peers = {};
+  for (int q = 0; q < world; ++q) {
+    if (q == rank) continue;
+    if (!d_peer_flags[q] || (reinterpret_cast<uintptr_t>(d_peer_flags[q]) & 3u))
+      return thork_set_error(THORK_ERR_INVALID, "peer_barrier: flags of rank %d NULL or unaligned",
+                             q);
+    peers.p[q] = static_cast<unsigned *>(d_peer_flags[q]);
+  }
+  if (world == 1) return THORK_OK;
+  unsigned *status;
+  int rc;
+  if ((rc = thork_status_word(&status))) return rc;
+  peer_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      peers, static_cast<unsigned *>(d_flags), world, rank, epoch, status);
+  return launch_check("peer_barrier launch");
 }
 
 namespace {

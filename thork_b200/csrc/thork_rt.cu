@@ -161,6 +161,9 @@ extern "C" int thork_device_attr(int dev, int attr, int *value) {
     case THORK_ATTR_L2_BYTES: a = cudaDevAttrL2CacheSize; break;
     case THORK_ATTR_CLOCK_KHZ: a = cudaDevAttrClockRate; break;
     case THORK_ATTR_MEM_CLOCK_KHZ: a = cudaDevAttrMemoryClockRate; break;
+    case THORK_ATTR_PCI_DOMAIN: a = cudaDevAttrPciDomainId; break;
+    case THORK_ATTR_PCI_BUS: a = cudaDevAttrPciBusId; break;
+    case THORK_ATTR_PCI_DEVICE: a = cudaDevAttrPciDeviceId; break;
     default: return thork_set_error(THORK_ERR_INVALID, "unknown attribute %d", attr);
   }
   CUDA_TRY(cudaDeviceGetAttribute(value, a, dev), "cudaDeviceGetAttribute");
@@ -278,6 +281,32 @@ extern "C" int thork_event_elapsed_ms(void *start, void *end, float *ms) {
 extern "C" int thork_stream_wait_event(void *stream, void *event) {
   CUDA_TRY(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), static_cast<cudaEvent_t>(event), 0),
            "cudaStreamWaitEvent");
+  return THORK_OK;
+}
+
+// ---------------------------------------------------------------------------
+// CUDA IPC (peer buffers of the fused GEMM + all-gather)
+// ---------------------------------------------------------------------------
+extern "C" int thork_ipc_handle(const void *d_ptr, void *handle64) {
+  if (!d_ptr || !handle64) return thork_set_error(THORK_ERR_INVALID, "ipc_handle: NULL argument");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  cudaIpcMemHandle_t h;
+  CUDA_TRY(cudaIpcGetMemHandle(&h, const_cast<void *>(d_ptr)), "cudaIpcGetMemHandle");
+  memcpy(handle64, &h, sizeof(h));
+  return THORK_OK;
+}
+
+extern "C" int thork_ipc_open(const void *handle64, void **d_ptr) {
+  if (!d_ptr || !handle64) return thork_set_error(THORK_ERR_INVALID, "ipc_open: NULL argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, sizeof(h));
+  CUDA_TRY(cudaIpcOpenMemHandle(d_ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+  return THORK_OK;
+}
+
+extern "C" int thork_ipc_close(void *d_ptr) {
+  if (!d_ptr) return THORK_OK;
+  CUDA_TRY(cudaIpcCloseMemHandle(d_ptr), "cudaIpcCloseMemHandle");
   return THORK_OK;
 }
 

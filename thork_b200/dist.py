@@ -15,6 +15,8 @@ hard-codes device 0, ``src/thork/runtime.py:85-105``).
 * ``sharded_matmul_host`` — the same from host arrays (pinned for full
   PCIe speed): this rank's A rows and B are copied in, C is gathered on the
   devices and this rank's rows are copied back.
+* ``FusedGather`` — the same bf16 product with the all-gather fused into
+  the GEMM epilogue (P2P stores over NVLink, then a device flag barrier).
 * decode shapes split W by contiguous N-column blocks (``col_shard``) with X
   replicated; gathered ``[G, M, N/G]`` blocks become ``M x N`` with
   ``assemble_col_blocks``.
@@ -118,6 +120,161 @@ class Communicator:
             self.handle = None
 
 
+class _View:
+    """A borrowed device pointer in the shape ``DeviceArray`` expects of its
+    buffer (no ownership)."""
+
+    __slots__ = ("ptr", "nbytes")
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.ptr, self.nbytes = int(ptr), int(nbytes)
+
+
+class FusedGather:
+    """Fused GEMM + all-gather over NVLink peer memory.
+
+    Every rank allocates, in one ``cudaMalloc``, ``slots`` full
+    ``m_total x n`` bf16 result buffers and a flag page, exports the
+    allocation with CUDA IPC and opens every peer's (the 64-byte handles and
+    each GPU's PCI location travel in one NCCL all-gather).  ``matmul`` runs
+    this rank's A rows through ``thork_gemm_bf16_allgather``: the GEMM's
+    epilogue stores each finished C tile into this GPU's result buffer and,
+    with P2P stores over NVLink, into the same rows of every peer's, so the
+    transfer overlaps the remaining tiles; a flag barrier kernel
+    (``thork_peer_barrier``) then orders every peer's stores before whatever
+    this rank queues next.  No NCCL call is on the data path.
+
+    Results rotate through the slots: consume a call's result (stream-ordered
+    on this rank) before making the next call.  Requires one GPU per rank
+    and at most 8 ranks.
+    """
+
+    SLOTS = 2
+
+    def __init__(self, comm: Communicator, m_total: int, n: int):
+        L = rt.lib()
+        self.comm = comm
+        self.rank, self.world = comm.rank, comm.world
+        if not (1 <= self.world <= 8):
+            raise ValueError(f"fused all-gather supports 1..8 ranks, got {self.world}")
+        self.m_total, self.n = int(m_total), int(n)
+        self.slot_bytes = ((self.m_total * self.n * 2 + 255) // 256) * 256
+        self.flag_off = self.SLOTS * self.slot_bytes
+        self.total_bytes = self.flag_off + 256
+        dev = rt.get_device()
+        base = ctypes.c_void_p()
+        rt.check(L.thork_malloc(self.total_bytes, ctypes.byref(base)), "fused gather buffer")
+        self.base = base.value
+        rt.check(L.thork_memset(self.base + self.flag_off, 0, 256, None), "flag page clear")
+        handle = (ctypes.c_uint8 * 64)()
+        rt.check(L.thork_ipc_handle(self.base, handle), "ipc handle")
+        loc = np.array([rt.device_attr(a, dev) for a in (7, 8, 9)] + [self.rank], dtype=np.int32)
+        mine = bytes(handle) + loc.tobytes()
+        rec = len(mine)
+        send = rt.DeviceArray((rec,), np.uint8)
+        recv = rt.DeviceArray((rec * self.world,), np.uint8)
+        rt.copy_htod(send.ptr, np.frombuffer(mine, np.uint8).copy())
+        comm.allgather(send.ptr, recv.ptr, rec, 0)
+        rt.check(L.thork_device_synchronize(), "synchronize")
+        allrec = recv.to_host().reshape(self.world, rec)
+        locs = [tuple(allrec[q, 64:].view(np.int32)[:3]) for q in range(self.world)]
+        if len(set(locs)) != self.world:
+            self._free_own()
+            raise RuntimeError("fused all-gather needs one GPU per rank; ranks share a GPU: "
+                               f"{locs}")
+        self.peer_base = [0] * self.world
+        self.peer_base[self.rank] = self.base
+        try:
+            for q in range(self.world):
+                if q == self.rank:
+                    continue
+                h = (ctypes.c_uint8 * 64).from_buffer_copy(allrec[q, :64].tobytes())
+                p = ctypes.c_void_p()
+                rt.check(L.thork_ipc_open(h, ctypes.byref(p)), f"ipc open (rank {q})")
+                self.peer_base[q] = p.value
+        except Exception:
+            self._close_peers()
+            self._free_own()
+            raise
+        self.peers = [q for q in range(self.world) if q != self.rank]
+        self.epoch = 0
+        self.calls = 0
+        self.flag_ptrs = (ctypes.c_void_p * 8)(*[b + self.flag_off for b in self.peer_base])
+        # every rank has opened every handle (and cleared its flags) before
+        # any peer store can arrive
+        comm.allgather(send.ptr, recv.ptr, rec, 0)
+        rt.check(L.thork_device_synchronize(), "synchronize")
+
+    def slot_ptr(self, slot: int, rank: Optional[int] = None) -> int:
+        b = self.base if rank is None else self.peer_base[rank]
+        return b + (slot % self.SLOTS) * self.slot_bytes
+
+    def result(self, slot: int) -> "rt.DeviceArray":
+        """The full ``m_total x n`` bf16 result held in ``slot`` on this rank."""
+        return rt.DeviceArray((self.m_total, self.n), np.uint16,
+                              buffer=_View(self.slot_ptr(slot), self.m_total * self.n * 2))
+
+    def barrier(self, stream: Optional[rt.Stream] = None) -> None:
+        """Device-side flag barrier over all ranks (stream-ordered)."""
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF
+        rt.check(rt.lib().thork_peer_barrier(self.base + self.flag_off, self.flag_ptrs,
+                                             self.world, self.rank, self.epoch,
+                                             stream.handle if stream else None), "peer barrier")
+
+    def matmul(self, a_local: "rt.DeviceArray", b: "rt.DeviceArray",
+               stream: Optional[rt.Stream] = None, gemm_done: Optional[rt.Event] = None, *,
+               dtype: str = "bf16", scale_a: float = 1.0,
+               scale_b: float = 1.0) -> "rt.DeviceArray":
+        """``C = A @ B`` with this rank holding rows ``row_shard(m_total)`` of
+        A (bf16, or e4m3 with C scaled by ``scale_a * scale_b``); returns
+        (stream-ordered) the full bf16 C on this rank."""
+        if dtype not in ("bf16", "e4m3"):
+            raise ValueError(f"unknown GEMM dtype {dtype!r}")
+        start, stop = row_shard(self.m_total, self.world, self.rank)
+        k = a_local.shape[1]
+        if a_local.shape[0] != stop - start or tuple(b.shape) != (k, self.n):
+            raise ValueError(f"shape mismatch: A rows {a_local.shape}, B {b.shape}, "
+                             f"shard {stop - start} x {k}, N {self.n}")
+        slot = self.calls % self.SLOTS
+        self.calls += 1
+        peers = (ctypes.c_void_p * 7)(*[self.slot_ptr(slot, q) for q in self.peers])
+        sh = stream.handle if stream else None
+        L = rt.lib()
+        args = (a_local.ptr, b.ptr, self.slot_ptr(slot), peers, len(self.peers), stop - start,
+                self.n, k, start)
+        if dtype == "bf16":
+            rc = L.thork_gemm_bf16_allgather(*args, 0, sh)
+        else:
+            rc = L.thork_gemm_e4m3_allgather(*args, float(scale_a), float(scale_b), 0, sh)
+        rt.check(rc, "fused gemm + all-gather")
+        if gemm_done is not None:
+            gemm_done.record(stream)
+        self.barrier(stream)
+        return self.result(slot)
+
+    def _close_peers(self) -> None:
+        for q, p in enumerate(getattr(self, "peer_base", [])):
+            if q != self.rank and p:
+                rt.lib().thork_ipc_close(p)
+                self.peer_base[q] = 0
+
+    def _free_own(self) -> None:
+        if getattr(self, "base", 0):
+            rt.lib().thork_free(self.base)
+            self.base = 0
+
+    def close(self) -> None:
+        """Collective: waits until no peer can still store here, then
+        releases the mappings and the buffer."""
+        if not getattr(self, "base", 0):
+            return
+        rt.check(rt.lib().thork_device_synchronize(), "synchronize")
+        self.barrier(None)
+        rt.check(rt.lib().thork_device_synchronize(), "synchronize")
+        self._close_peers()
+        self._free_own()
+
+
 def _gemm_launcher(dtype: str, m: int, n: int, k: int, scale: float = 1.0) -> Callable:
     L = rt.lib()
     if dtype == "bf16":
@@ -181,14 +338,23 @@ _staging = _HostStaging()
 
 def sharded_matmul_host(comm: Optional[Communicator], a_rows: np.ndarray, b: np.ndarray,
                         c_rows: np.ndarray, m_total: int, *, dtype: str = "bf16",
-                        scale: float = 1.0) -> None:
+                        scale: float = 1.0, fused: Optional[FusedGather] = None) -> None:
     """Host-array form of ``sharded_matmul``: copies this rank's A rows and B
-    to the device, computes and all-gathers C on the devices, and copies this
-    rank's rows of C back into ``c_rows``.  Synchronous."""
+    to the device, computes and all-gathers C on the devices (through
+    ``fused`` when given, else NCCL), and copies this rank's rows of C back
+    into ``c_rows``.  Synchronous."""
     stream = rt._dispatch_stream()
     a_dev = _staging.get("a", a_rows.shape, a_rows.dtype)
     b_dev = _staging.get("b", b.shape, b.dtype)
     world = comm.world if comm is not None else 1
+    if fused is not None and world > 1:
+        rt.copy_htod(a_dev.ptr, np.ascontiguousarray(a_rows), stream, sync=False)
+        rt.copy_htod(b_dev.ptr, np.ascontiguousarray(b), stream, sync=False)
+        c = fused.matmul(a_dev, b_dev, stream, dtype=dtype, scale_a=scale)
+        start, _ = row_shard(m_total, world, comm.rank)
+        rt.copy_dtoh(c_rows, c.ptr + start * b.shape[1] * 2, stream, sync=False)
+        stream.synchronize()
+        return
     rows_out = m_total if world > 1 else a_rows.shape[0]
     c_dev = _staging.get("c", (rows_out, b.shape[1]), np.uint16)
     rt.copy_htod(a_dev.ptr, np.ascontiguousarray(a_rows), stream, sync=False)

@@ -91,6 +91,13 @@ _SIGNATURES = {
     "thork_gemm_e4m3": [_vp, _vp, _vp, _i, _i, _i, ctypes.c_float, ctypes.c_float, _i, _vp],
     "thork_skinny_gemm_bf16": [_vp, _vp, _vp, _i, _i, _i, _vp],
     "thork_skinny_gemm_bf16_noalloc": [_vp, _vp, _vp, _i, _i, _i, _vp],
+    "thork_gemm_bf16_allgather": [_vp, _vp, _vp, _pvp, _i, _i, _i, _i, _i, _i, _vp],
+    "thork_gemm_e4m3_allgather": [_vp, _vp, _vp, _pvp, _i, _i, _i, _i, _i, ctypes.c_float,
+                                  ctypes.c_float, _i, _vp],
+    "thork_peer_barrier": [_vp, _pvp, _i, _i, ctypes.c_uint, _vp],
+    "thork_ipc_handle": [_vp, _vp],
+    "thork_ipc_open": [_vp, _pvp],
+    "thork_ipc_close": [_vp],
     "thork_nccl_get_unique_id": [_vp],
     "thork_nccl_comm_init_rank": [_pvp, _i, _vp, _i],
     "thork_nccl_comm_destroy": [_vp],
