@@ -217,21 +217,29 @@ THORK_API int thork_skinny_gemm_bf16(const void *d_x, const void *d_w, void *d_y
 /* C[M,N] rows [row0, row0+rows) = A_rows . B, written both to d_c (this
  * GPU's full M x N result buffer) and, over NVLink, to the same rows of each
  * peer's result buffer d_peer_c[0..n_peers) (pointers opened with
- * thork_ipc_open).  This fuses the GEMM with the all-gather of C: after all
- * ranks' launches complete (e.g. behind an NCCL all-reduce used as a
- * barrier), every rank holds the full C.  bf16 in/out, same constraints and
- * variants as thork_gemm_bf16, at most 7 peers.  No reference counterpart
- * (the reference is single-GPU, src/thork/runtime.py:85-105).             */
+ * thork_ipc_open).  This fuses the GEMM with the all-gather of C: once every
+ * rank's launch is complete (thork_peer_barrier), every rank holds the full
+ * C.  bf16 in/out, K and N multiples of 8, at most 7 peers.
+ * variant 1: the epilogue stores each tile to the peers itself;
+ * variant 2: four extra warps per CTA share all (tile, peer) pushes of the
+ *   grid (cooperative launch); needs d_tile_flags, ceil(rows/128) *
+ *   ceil(N/256) zero-initialised words owned by this GPU, and `epoch` =
+ *   1, 2, 3, ... for successive calls on the same flags (variant 1 also
+ *   counts on the flags when they are given, so calls may mix variants);
+ * variant 0: 2 when n_peers >= 3, else 1.
+ * No reference counterpart (the reference is single-GPU,
+ * src/thork/runtime.py:85-105).                                            */
 THORK_API int thork_gemm_bf16_allgather(const void *d_a_rows, const void *d_b, void *d_c,
                                         void *const *d_peer_c, int n_peers, int rows, int N, int K,
-                                        int row0, int variant, void *stream);
+                                        int row0, unsigned *d_tile_flags, unsigned epoch,
+                                        int variant, void *stream);
 /* FP8 form of thork_gemm_bf16_allgather: e4m3 A rows and B (K, N multiples
  * of 16), C = scale_a * scale_b * A.B in bf16 rows on this GPU and every
  * peer.  No reference counterpart.                                         */
 THORK_API int thork_gemm_e4m3_allgather(const void *d_a_rows, const void *d_b, void *d_c,
                                         void *const *d_peer_c, int n_peers, int rows, int N, int K,
-                                        int row0, float scale_a, float scale_b, int variant,
-                                        void *stream);
+                                        int row0, unsigned *d_tile_flags, unsigned epoch,
+                                        float scale_a, float scale_b, int variant, void *stream);
 /* Device-side barrier of the fused all-gather: this rank stores `epoch` into
  * slot `rank` of every peer's flag array (d_peer_flags[q], q != rank, each
  * `world` unsigned words in the peer's memory opened with thork_ipc_open)

@@ -62,13 +62,18 @@ def test_library_kernels_reject_bad_shapes_before_touching_a_device():
 def test_fused_allgather_and_barrier_reject_bad_arguments_on_the_host():
     L = rt.lib()
     peers = (ctypes.c_void_p * 7)(*([32] * 7))
-    assert L.thork_gemm_bf16_allgather(16, 16, 16, peers, 8, 64, 64, 64, 0, 0, None) == rt.ERR_INVALID
+
+    def ag(n_peers, row0=0, variant=0, p=peers, flags=None):
+        return L.thork_gemm_bf16_allgather(16, 16, 16, p, n_peers, 64, 64, 64, row0, flags, 1,
+                                           variant, None)
+    assert ag(8) == rt.ERR_INVALID
     assert "n_peers" in rt.last_error()
-    assert L.thork_gemm_bf16_allgather(16, 16, 16, peers, 1, 64, 64, 64, 0, 2, None) == rt.ERR_INVALID
+    assert ag(1, variant=3) == rt.ERR_INVALID
     assert "variant" in rt.last_error()
-    bad = (ctypes.c_void_p * 7)(*([40] * 7))  # not 16-byte aligned
-    assert L.thork_gemm_bf16_allgather(16, 16, 16, bad, 1, 64, 64, 64, 0, 0, None) == rt.ERR_INVALID
-    assert L.thork_gemm_bf16_allgather(16, 16, 16, peers, 1, 64, 64, 64, -1, 0, None) == rt.ERR_INVALID
+    assert ag(1, p=(ctypes.c_void_p * 7)(*([40] * 7))) == rt.ERR_INVALID  # not 16-byte aligned
+    assert ag(1, row0=-1) == rt.ERR_INVALID
+    assert ag(3, variant=2) == rt.ERR_INVALID  # push variant without tile flags
+    assert "tile flags" in rt.last_error()
     flags = (ctypes.c_void_p * 8)()
     assert L.thork_peer_barrier(16, flags, 9, 0, 1, None) == rt.ERR_INVALID
     assert L.thork_peer_barrier(16, flags, 2, 2, 1, None) == rt.ERR_INVALID

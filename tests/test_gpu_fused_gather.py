@@ -55,7 +55,7 @@ def _rank(rank, world, port, q):
                 a16 = oracle.f32_to_bf16_bits(a)
                 s, e = dist.row_shard(m, world, rank)
                 A = rt.to_device(np.ascontiguousarray(a16[s:e]))
-                C = fg.matmul(A, B, stream)
+                C = fg.matmul(A, B, stream, variant=1 + call % 2)
                 got = C.to_host(stream=stream)  # consumed before the next call
                 err = oracle.max_rel_err(oracle.bf16_bits_to_f32(got), oracle.gemm_bf16_ref(a16, b))
                 assert err <= 1e-2, f"rank {rank} call {call} {m}x{n}x{k}: max rel err {err}"
@@ -120,22 +120,30 @@ def test_fused_epilogue_on_one_gpu_writes_every_destination(dtype):
     dests = [rt.to_device(np.full((m_total, n), 0x7E7E, np.uint16)) for _ in range(3)]
     plain = rt.empty((rows, n), np.uint16)
     peers = (ctypes.c_void_p * 7)(dests[1].ptr, dests[2].ptr)
+    flags = rt.empty((((rows + 127) // 128) * ((n + 255) // 256),), np.uint32)
+    flags.zero()
     if dtype == "bf16":
-        rt.check(L.thork_gemm_bf16_allgather(A.ptr, B.ptr, dests[0].ptr, peers, 2, rows, n, k, row0,
-                                             0, None))
         rt.check(L.thork_gemm_bf16(A.ptr, B.ptr, plain.ptr, rows, n, k, 1, None))
     else:
-        rt.check(L.thork_gemm_e4m3_allgather(A.ptr, B.ptr, dests[0].ptr, peers, 2, rows, n, k, row0,
-                                             sa, sb, 0, None))
         rt.check(L.thork_gemm_e4m3(A.ptr, B.ptr, plain.ptr, rows, n, k, sa, sb, 1, None))
-    rt.synchronize()
-    assert rt.kernel_status() == 0
     want = plain.to_host()
     assert oracle.max_rel_err(oracle.bf16_bits_to_f32(want), ref) <= 1e-2
-    for d in dests:
-        got = d.to_host()
-        np.testing.assert_array_equal(got[row0:row0 + rows], want)
-        assert (got[:row0] == 0x7E7E).all() and (got[row0 + rows:] == 0x7E7E).all()
+    # both all-gather variants in turn on the same tile flags
+    for epoch, variant in ((1, 1), (2, 2), (3, 2), (4, 1)):
+        for d in dests:
+            rt.check(L.thork_memset(d.ptr, 0x7E, d.nbytes, None))
+        if dtype == "bf16":
+            rt.check(L.thork_gemm_bf16_allgather(A.ptr, B.ptr, dests[0].ptr, peers, 2, rows, n, k,
+                                                 row0, flags.ptr, epoch, variant, None))
+        else:
+            rt.check(L.thork_gemm_e4m3_allgather(A.ptr, B.ptr, dests[0].ptr, peers, 2, rows, n, k,
+                                                 row0, flags.ptr, epoch, sa, sb, variant, None))
+        rt.synchronize()
+        assert rt.kernel_status() == 0, (epoch, variant)
+        for d in dests:
+            got = d.to_host()
+            np.testing.assert_array_equal(got[row0:row0 + rows], want)
+            assert (got[:row0] == 0x7E7E).all() and (got[row0 + rows:] == 0x7E7E).all()
 
 
 def test_fused_gemm_allgather_over_peer_memory():

@@ -54,12 +54,12 @@ struct Config {
   // stages + barriers (full/empty per stage, tmem full/empty x2, teardown) + tmem slot
   static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
-  // fused all-gather epilogue: each epilogue warp stages 32 rows x EPI_COLS
+  // staged all-gather epilogue: each epilogue warp stages 32 rows x EPI_COLS
   // bf16 in shared memory so that its global stores are whole 128-byte lines
   static constexpr int EPI_COLS = 64;
   static constexpr int EPI_OFF = STAGES * STAGE_BYTES + ((BAR_BYTES + 127) & ~127);
   static constexpr int EPI_WARP_BYTES = 32 * EPI_COLS * 2;
-  static constexpr int SMEM_BYTES_PEERS = 1024 + EPI_OFF + 4 * EPI_WARP_BYTES;
+  static constexpr int SMEM_BYTES_STAGED = 1024 + EPI_OFF + 4 * EPI_WARP_BYTES;
   static constexpr u32 IDESC =
       make_idesc(KIND == KIND_BF16 ? 1u : 0u, KIND == KIND_BF16 ? 1u : 0u, A_MN, B_MN, BM, BN);
 
@@ -68,11 +68,6 @@ struct Config {
   static_assert(!B_MN || BN % CHUNK == 0, "MN-major B needs BN multiple of the 128-byte chunk");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
 };
-
-template <class Cfg, bool PEERS>
-constexpr int smem_bytes() {
-  return PEERS ? Cfg::SMEM_BYTES_PEERS : Cfg::SMEM_BYTES;
-}
 
 struct Params {
   void *out;      // bf16 output
@@ -86,7 +81,21 @@ struct Params {
   // offsets of up to 7 peer GPUs' buffers (P2P stores over NVLink)
   void *peer[7];
   int npeer;
+  u32 *tile_flags;  // push-warp all-gather: per-tile completion counts
+  u32 epoch;        // this call's number: tile t is done once flags[t] == 4 * epoch
 };
+
+// Modes of the fused all-gather inside gemm_kernel.
+enum : int { AG_NONE = 0, AG_STAGED = 1, AG_PUSH = 2 };
+
+template <class Cfg, int AG>
+constexpr int gemm_smem_bytes() {
+  return AG == AG_STAGED ? Cfg::SMEM_BYTES_STAGED : Cfg::SMEM_BYTES;
+}
+template <class Cfg, int AG>
+constexpr int gemm_threads() {
+  return AG == AG_PUSH ? Cfg::THREADS + 128 : Cfg::THREADS;
+}
 
 // Output-tile order: groups of GROUP_M tile-rows walked column by column, so
 // the ~SM-count tiles in flight share A rows and B columns in L2.
@@ -226,8 +235,81 @@ __device__ __forceinline__ void bf16_store_tile_peers(const Params &p, u32 t_row
   }
 }
 
-template <class Cfg, bool PEERS = false>
-__global__ void __launch_bounds__(192, 1)
+// Push warps of the AG_PUSH all-gather (warps 6..9).  The (tile, peer)
+// pushes of the whole grid, in tile order, are dealt round-robin to the
+// CTAs, so every SM carries an equal share of the NVLink traffic whichever
+// SM computed the tile.  A push waits (bounded) until the four epilogue
+// warps of the tile's CTA have stored it to this GPU's C (tile_flags[t]
+// reaches 4 * epoch), reads it back from L2 and stores it to the peer's C
+// at the same offset, one 512-byte row segment per warp instruction.  The
+// epilogue never waits for the pushes.  All CTAs are co-resident (a
+// cooperative launch), so a wait on another CTA's tile always ends.
+template <class Cfg>
+__device__ __forceinline__ void push_tasks(const Params &p, int ntm, int ntn, int ntiles,
+                                           volatile u32 *abort_flag, int pw, int lane) {
+  static_assert(Cfg::BN == 256, "one 16-byte chunk per lane covers a 256-column tile row");
+  const unsigned short *out = static_cast<const unsigned short *>(p.out);
+  const int ntasks = ntiles * p.npeer;
+  const u32 need = 4u * p.epoch;
+  for (int j = blockIdx.x; j < ntasks; j += gridDim.x) {
+    const int t = j / p.npeer, g = j - t * p.npeer;
+    int ok = 1;
+    if (lane == 0) {
+      const u64 t0 = globaltimer();
+      for (;;) {
+        u32 v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p.tile_flags + t) : "memory");
+        if (static_cast<int>(v - need) >= 0) break;
+        if (*abort_flag) { ok = 0; break; }
+        if (globaltimer() - t0 > THORK_WAIT_TIMEOUT_NS) {
+          report_status(p.status, STATUS_WAIT_TIMEOUT, 7);
+          *abort_flag = 1;
+          ok = 0;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+    int tm, tn;
+    tile_coords<Cfg::GROUP_M>(t, ntm, ntn, tm, tn);
+    const int col = tn * Cfg::BN + lane * 8;
+    // N is a multiple of 8, so a lane's 16-byte chunk is wholly in or out
+    const int row_end = col < p.out_cols ? min(tm * Cfg::BM + Cfg::BM, p.out_rows) : 0;
+    unsigned short *dst = nullptr;
+#pragma unroll
+    for (int q = 0; q < 7; ++q)  // constant indices keep p.peer in parameter space
+      if (q == g) dst = static_cast<unsigned short *>(p.peer[q]);
+#pragma unroll 1
+    for (int r0 = tm * Cfg::BM + pw; r0 < row_end; r0 += 32) {
+      // eight rows in flight: r0, r0+4, ..., r0+28 of this warp's share
+      uint4 v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int row = r0 + 4 * i;
+        if (row < row_end) {
+          const unsigned short *src = out + static_cast<long long>(row) * p.ldo + col;
+          asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(v[i].x), "=r"(v[i].y), "=r"(v[i].z), "=r"(v[i].w)
+                       : "l"(src));
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int row = r0 + 4 * i;
+        if (row < row_end)
+          st_global_v4(dst + static_cast<long long>(row) * p.ldo + col, v[i].x, v[i].y, v[i].z,
+                       v[i].w);
+      }
+    }
+  }
+  // these stores are ordered before anything a later kernel signals to the
+  // peers (the fused all-gather's flag barrier)
+  __threadfence_system();
+}
+
+template <class Cfg, int AG = AG_NONE>
+__global__ void __launch_bounds__(gemm_threads<Cfg, AG>(), 1)
     gemm_kernel(const __grid_constant__ TensorMap tmap_a, const __grid_constant__ TensorMap tmap_b,
                 const Params p) {
   pdl_launch_dependents();
@@ -370,6 +452,9 @@ __global__ void __launch_bounds__(192, 1)
       mbar_wait(drain_bar, 0, p.status, 5);
     }
     __syncwarp();
+  } else if (warp >= 6) {
+    // ------------------------------------------------ NVLink push (warps 6..9)
+    if constexpr (AG == AG_PUSH) push_tasks<Cfg>(p, ntm, ntn, ntiles, abort_flag, warp - 6, lane);
   } else {
     // ------------------------------------------------ epilogue (warps 2..5)
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
@@ -388,7 +473,7 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const int row_mma = tm * Cfg::BM + q * 32 + lane;  // MMA-space row owned by this thread
       const u32 t_row = tmem_base + ((u32)(q * 32) << 16) + acc * Cfg::BN;
-      if constexpr (PEERS)
+      if constexpr (AG == AG_STAGED)
         bf16_store_tile_peers<Cfg>(p, t_row, tm * Cfg::BM + q * 32, tn * Cfg::BN,
                                    smem + Cfg::EPI_OFF + q * Cfg::EPI_WARP_BYTES, lane);
       else
@@ -396,10 +481,19 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(acc));
+      if constexpr (AG != AG_NONE) {
+        // the warp's rows of this tile are in C: publish them to the push
+        // warps (counted in both modes, so epochs stay in step when calls
+        // on the same flags mix the variants)
+        if (lane == 0 && p.tile_flags) {
+          __threadfence();
+          asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.tile_flags + t) : "memory");
+        }
+      }
     }
-    // peer stores are ordered before anything a later kernel signals to
-    // the peers (the fused all-gather's flag barrier)
-    if constexpr (PEERS) __threadfence_system();
+    // staged peer stores are ordered before anything a later kernel signals
+    // to the peers (the fused all-gather's flag barrier)
+    if constexpr (AG == AG_STAGED) __threadfence_system();
   }
 
   tc_fence_before();
@@ -711,12 +805,6 @@ struct Config2 {
   static constexpr int THREADS = 192;
   static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
-  // fused all-gather epilogue: each epilogue warp stages 32 rows x EPI_COLS
-  // bf16 in shared memory so that its global stores are whole 128-byte lines
-  static constexpr int EPI_COLS = 64;
-  static constexpr int EPI_OFF = STAGES * STAGE_BYTES + ((BAR_BYTES + 127) & ~127);
-  static constexpr int EPI_WARP_BYTES = 32 * EPI_COLS * 2;
-  static constexpr int SMEM_BYTES_PEERS = 1024 + EPI_OFF + 4 * EPI_WARP_BYTES;
   static constexpr u32 IDESC =
       make_idesc(KIND == KIND_BF16 ? 1u : 0u, KIND == KIND_BF16 ? 1u : 0u, false, true, 256, BN);
   static_assert(BN % 32 == 0 && BN <= 256, "pair tile N must be a multiple of 32, at most 256");

@@ -194,18 +194,24 @@ extern "C" int thork_matrix_add_f32(float *d_out, const float *d_a, const float 
 // tcgen05 GEMMs
 // ---------------------------------------------------------------------------
 // Launch with programmatic stream serialisation (the kernel executes
-// griddepcontrol.wait before touching global memory) and an optional
-// cluster of `cluster_x` CTAs.
+// griddepcontrol.wait before touching global memory), an optional cluster
+// of `cluster_x` CTAs, and optionally as a cooperative grid (all CTAs
+// co-resident, for kernels whose CTAs wait on one another).
 template <class... KArgs, class... Args>
 static int launch_pdl(void (*kern)(KArgs...), dim3 grid, int threads, int smem, cudaStream_t s,
-                      int cluster_x, const char *name, Args &&...args) {
+                      int cluster_x, bool cooperative, const char *name, Args &&...args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(threads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[2];
+  cudaLaunchAttribute attr[3];
   int n = 0;
+  if (cooperative) {
+    attr[n].id = cudaLaunchAttributeCooperative;
+    attr[n].val.cooperative = 1;
+    ++n;
+  }
   attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[n].val.programmaticStreamSerializationAllowed = 1;
   ++n;
@@ -242,21 +248,24 @@ using CfgSkinny256 = Config<KIND_BF16, 256, 4, true, false, true>;
 
 enum KernelId {
   K_GEMM_BF16 = 0, K_GEMM_E4M3, K_SKINNY16, K_SKINNY32, K_SKINNY64, K_SKINNY128, K_SKINNY256,
-  K_GEMM2_BF16, K_GEMM2_E4M3, K_SKSK16, K_SKSK32, K_GEMM_BF16_AG, K_GEMM_E4M3_AG
+  K_GEMM2_BF16, K_GEMM2_E4M3, K_SKSK16, K_SKSK32, K_GEMM_BF16_AG, K_GEMM_E4M3_AG,
+  K_GEMM_BF16_AGP, K_GEMM_E4M3_AGP
 };
 
-template <class Cfg, bool PEERS = false>
+template <class Cfg, int AG = AG_NONE>
 int run_gemm(int kernel_id, const TensorMap &ta, const TensorMap &tb, const Params &prm,
              cudaStream_t s, const char *name) {
   int rc, sms;
-  auto kern = gemm_kernel<Cfg, PEERS>;
-  constexpr int smem = smem_bytes<Cfg, PEERS>();
+  auto kern = gemm_kernel<Cfg, AG>;
+  constexpr int smem = gemm_smem_bytes<Cfg, AG>();
   static_assert(smem <= 232448, "shared memory budget exceeded");
   if ((rc = ensure_smem(reinterpret_cast<const void *>(kern), kernel_id, smem))) return rc;
   if ((rc = thork_sm_count(&sms))) return rc;
   const int ntiles = ((prm.GM + Cfg::BM - 1) / Cfg::BM) * ((prm.GN + Cfg::BN - 1) / Cfg::BN);
   const int grid = ntiles < sms ? ntiles : sms;
-  return launch_pdl(kern, dim3(grid), Cfg::THREADS, smem, s, 1, name, ta, tb, prm);
+  // push warps wait on tiles of other CTAs: launch the grid co-resident
+  return launch_pdl(kern, dim3(grid), gemm_threads<Cfg, AG>(), smem, s, 1, AG == AG_PUSH, name, ta,
+                    tb, prm);
 }
 
 // Cluster-pair launch: grid = 2 x (pairs), cluster (2,1,1).
@@ -269,7 +278,8 @@ int run_gemm2(int kernel_id, const TensorMap &ta, const TensorMap &tb, const Par
   if ((rc = thork_sm_count(&sms))) return rc;
   const int ntiles = ((prm.GM + 2 * Cfg::BM - 1) / (2 * Cfg::BM)) * ((prm.GN + Cfg::BN - 1) / Cfg::BN);
   const int pairs = ntiles < sms / 2 ? ntiles : sms / 2;
-  return launch_pdl(kern, dim3(2 * pairs), Cfg::THREADS, Cfg::SMEM_BYTES, s, 2, name, ta, tb, prm);
+  return launch_pdl(kern, dim3(2 * pairs), Cfg::THREADS, Cfg::SMEM_BYTES, s, 2, false, name, ta, tb,
+                    prm);
 }
 
 int check_dims(int M, int N, int K, int align, const char *what) {
@@ -348,17 +358,19 @@ extern "C" int thork_gemm_e4m3(const void *d_a, const void *d_b, void *d_c, int 
 namespace {
 // Shared body of the fused GEMM + all-gather entry points: this rank's rows
 // [row0, row0 + rows) of C go to d_c and to every peer buffer at the same
-// offset (1-CTA kernel with the peer-store epilogue).
+// offset.  Variant 1 stores to the peers from the epilogue (through a
+// shared-memory staging tile); variant 2 leaves that to four push warps per
+// CTA that share all (tile, peer) pushes of the grid; 0 chooses.
 template <class Cfg>
-int gemm_allgather(int kernel_id, int dt, int elem, const void *d_a_rows, const void *d_b,
-                   void *d_c, void *const *d_peer_c, int n_peers, int rows, int N, int K, int row0,
-                   float alpha, int variant, void *stream, const char *what) {
+int gemm_allgather(int kid_staged, int kid_push, int dt, int elem, const void *d_a_rows,
+                   const void *d_b, void *d_c, void *const *d_peer_c, int n_peers, int rows, int N,
+                   int K, int row0, unsigned *d_tile_flags, unsigned epoch, float alpha,
+                   int variant, void *stream, const char *what) {
   int rc;
   if ((rc = check_dims(rows, N, K, 16 / elem, what))) return rc;
   if ((rc = check_ptrs(d_a_rows, d_b, d_c, what))) return rc;
-  if (variant < 0 || variant > 1)
-    return thork_set_error(THORK_ERR_INVALID, "%s: variant %d not supported (0 or 1)", what,
-                           variant);
+  if (variant < 0 || variant > 2)
+    return thork_set_error(THORK_ERR_INVALID, "%s: unknown variant %d", what, variant);
   if (n_peers < 0 || n_peers > 7 || (n_peers > 0 && !d_peer_c))
     return thork_set_error(THORK_ERR_INVALID, "%s: n_peers=%d must be 0..7", what, n_peers);
   if (row0 < 0) return thork_set_error(THORK_ERR_INVALID, "%s: row0 < 0", what);
@@ -366,6 +378,10 @@ int gemm_allgather(int kernel_id, int dt, int elem, const void *d_a_rows, const 
     if (!d_peer_c[g] || (reinterpret_cast<uintptr_t>(d_peer_c[g]) & 15u))
       return thork_set_error(THORK_ERR_INVALID,
                              "%s: peer buffer %d is NULL or not 16-byte aligned", what, g);
+  if (variant == 0) variant = n_peers >= 3 ? 2 : 1;
+  if (variant == 2 && (!d_tile_flags || (reinterpret_cast<uintptr_t>(d_tile_flags) & 3u)))
+    return thork_set_error(THORK_ERR_INVALID, "%s: variant 2 needs 4-byte aligned tile flags",
+                           what);
   alignas(64) TensorMap ta, tb;
   if ((rc = thork_encode_tmap_2d(&ta, dt, d_a_rows, rows, K, (uint64_t)K * elem, Cfg::BM, Cfg::BK,
                                  128)))
@@ -378,25 +394,30 @@ int gemm_allgather(int kernel_id, int dt, int elem, const void *d_a_rows, const 
   Params prm{static_cast<char *>(d_c) + off, rows, N, K, N, rows, N, alpha, status};
   for (int g = 0; g < n_peers; ++g) prm.peer[g] = static_cast<char *>(d_peer_c[g]) + off;
   prm.npeer = n_peers;
-  return run_gemm<Cfg, true>(kernel_id, ta, tb, prm, static_cast<cudaStream_t>(stream), what);
+  prm.tile_flags = d_tile_flags;
+  prm.epoch = epoch;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (variant == 2) return run_gemm<Cfg, AG_PUSH>(kid_push, ta, tb, prm, s, what);
+  return run_gemm<Cfg, AG_STAGED>(kid_staged, ta, tb, prm, s, what);
 }
 }  // namespace
 
 extern "C" int thork_gemm_bf16_allgather(const void *d_a_rows, const void *d_b, void *d_c,
                                         void *const *d_peer_c, int n_peers, int rows, int N, int K,
-                                        int row0, int variant, void *stream) {
-  return gemm_allgather<CfgBf16>(K_GEMM_BF16_AG, THORK_DT_BF16, 2, d_a_rows, d_b, d_c, d_peer_c,
-                                 n_peers, rows, N, K, row0, 1.0f, variant, stream,
-                                 "gemm_bf16_allgather");
+                                        int row0, unsigned *d_tile_flags, unsigned epoch,
+                                        int variant, void *stream) {
+  return gemm_allgather<CfgBf16>(K_GEMM_BF16_AG, K_GEMM_BF16_AGP, THORK_DT_BF16, 2, d_a_rows, d_b,
+                                 d_c, d_peer_c, n_peers, rows, N, K, row0, d_tile_flags, epoch,
+                                 1.0f, variant, stream, "gemm_bf16_allgather");
 }
 
 extern "C" int thork_gemm_e4m3_allgather(const void *d_a_rows, const void *d_b, void *d_c,
                                         void *const *d_peer_c, int n_peers, int rows, int N, int K,
-                                        int row0, float scale_a, float scale_b, int variant,
-                                        void *stream) {
-  return gemm_allgather<CfgE4m3>(K_GEMM_E4M3_AG, THORK_DT_E4M3, 1, d_a_rows, d_b, d_c, d_peer_c,
-                                 n_peers, rows, N, K, row0, scale_a * scale_b, variant, stream,
-                                 "gemm_e4m3_allgather");
+                                        int row0, unsigned *d_tile_flags, unsigned epoch,
+                                        float scale_a, float scale_b, int variant, void *stream) {
+  return gemm_allgather<CfgE4m3>(K_GEMM_E4M3_AG, K_GEMM_E4M3_AGP, THORK_DT_E4M3, 1, d_a_rows, d_b,
+                                 d_c, d_peer_c, n_peers, rows, N, K, row0, d_tile_flags, epoch,
+                                 scale_a * scale_b, variant, stream, "gemm_e4m3_allgather");
 }
 
 namespace {
@@ -540,7 +561,7 @@ int launch_skinny_sk(int kernel_id, const TensorMap &ta, const TensorMap &tb, co
   sp.base = pl.base;
   sp.extra = pl.extra;
   sp.max_seg = pl.max_seg;
-  return launch_pdl(kern, dim3(pl.grid), Cfg::THREADS, Cfg::SMEM_BYTES, s, 1, "skinny_sk_kernel launch",
+  return launch_pdl(kern, dim3(pl.grid), Cfg::THREADS, Cfg::SMEM_BYTES, s, 1, false, "skinny_sk_kernel launch",
                     ta, tb, sp);
 }
 

@@ -199,6 +199,12 @@ class FusedGather:
         self.peers = [q for q in range(self.world) if q != self.rank]
         self.epoch = 0
         self.calls = 0
+        # per-tile completion counts of the push-warp variant (this GPU only)
+        rows = max(e - s for s, e in (row_shard(self.m_total, self.world, q)
+                                      for q in range(self.world)))
+        self.tile_flags = rt.DeviceArray((((rows + 127) // 128) * ((self.n + 255) // 256),),
+                                         np.uint32)
+        self.tile_flags.zero()
         self.flag_ptrs = (ctypes.c_void_p * 8)(*[b + self.flag_off for b in self.peer_base])
         # every rank has opened every handle (and cleared its flags) before
         # any peer store can arrive
@@ -223,8 +229,8 @@ class FusedGather:
 
     def matmul(self, a_local: "rt.DeviceArray", b: "rt.DeviceArray",
                stream: Optional[rt.Stream] = None, gemm_done: Optional[rt.Event] = None, *,
-               dtype: str = "bf16", scale_a: float = 1.0,
-               scale_b: float = 1.0) -> "rt.DeviceArray":
+               dtype: str = "bf16", scale_a: float = 1.0, scale_b: float = 1.0,
+               variant: int = 0) -> "rt.DeviceArray":
         """``C = A @ B`` with this rank holding rows ``row_shard(m_total)`` of
         A (bf16, or e4m3 with C scaled by ``scale_a * scale_b``); returns
         (stream-ordered) the full bf16 C on this rank."""
@@ -236,16 +242,16 @@ class FusedGather:
             raise ValueError(f"shape mismatch: A rows {a_local.shape}, B {b.shape}, "
                              f"shard {stop - start} x {k}, N {self.n}")
         slot = self.calls % self.SLOTS
-        self.calls += 1
+        self.calls += 1  # also the epoch of the tile flags
         peers = (ctypes.c_void_p * 7)(*[self.slot_ptr(slot, q) for q in self.peers])
         sh = stream.handle if stream else None
         L = rt.lib()
         args = (a_local.ptr, b.ptr, self.slot_ptr(slot), peers, len(self.peers), stop - start,
-                self.n, k, start)
+                self.n, k, start, self.tile_flags.ptr, self.calls & 0xFFFFFFFF)
         if dtype == "bf16":
-            rc = L.thork_gemm_bf16_allgather(*args, 0, sh)
+            rc = L.thork_gemm_bf16_allgather(*args, int(variant), sh)
         else:
-            rc = L.thork_gemm_e4m3_allgather(*args, float(scale_a), float(scale_b), 0, sh)
+            rc = L.thork_gemm_e4m3_allgather(*args, float(scale_a), float(scale_b), int(variant), sh)
         rt.check(rc, "fused gemm + all-gather")
         if gemm_done is not None:
             gemm_done.record(stream)
