@@ -223,8 +223,8 @@ THORK_API int thork_skinny_gemm_bf16(const void *d_x, const void *d_w, void *d_y
  * variant 1: the epilogue stores each tile to the peers itself;
  * variant 2: four extra warps per CTA share all (tile, peer) pushes of the
  *   grid (cooperative launch); needs d_tile_flags, ceil(rows/128) *
- *   ceil(N/256) zero-initialised words owned by this GPU, and `epoch` =
- *   1, 2, 3, ... for successive calls on the same flags (variant 1 also
+ *   ceil(N/64) zero-initialised words owned by this GPU, and `epoch` =
+ *   1, 2, 3, ... for successive calls on the same flags (every variant
  *   counts on the flags when they are given, so calls may mix variants);
  * variant 0: 2 when n_peers >= 3, else 1.
  * No reference counterpart (the reference is single-GPU,

@@ -81,8 +81,8 @@ struct Params {
   // offsets of up to 7 peer GPUs' buffers (P2P stores over NVLink)
   void *peer[7];
   int npeer;
-  u32 *tile_flags;  // push-warp all-gather: per-tile completion counts
-  u32 epoch;        // this call's number: tile t is done once flags[t] == 4 * epoch
+  u32 *tile_flags;  // fused all-gather: completion counts per 128 x 64 unit of C
+  u32 epoch;        // this call's number: a unit is done once its count is 4 * epoch
 };
 
 // Modes of the fused all-gather inside gemm_kernel.
@@ -239,26 +239,31 @@ __device__ __forceinline__ void bf16_store_tile_peers(const Params &p, u32 t_row
 // pushes of the whole grid, in tile order, are dealt round-robin to the
 // CTAs, so every SM carries an equal share of the NVLink traffic whichever
 // SM computed the tile.  A push waits (bounded) until the four epilogue
-// warps of the tile's CTA have stored it to this GPU's C (tile_flags[t]
-// reaches 4 * epoch), reads it back from L2 and stores it to the peer's C
+// warps of the tile's CTA have stored it to this GPU's C (the count of its
+// first 128 x 64 unit reaches 4 * epoch), reads it back from L2 and stores it to the peer's C
 // at the same offset, one 512-byte row segment per warp instruction.  The
 // epilogue never waits for the pushes.  All CTAs are co-resident (a
 // cooperative launch), so a wait on another CTA's tile always ends.
 template <class Cfg>
 __device__ __forceinline__ void push_tasks(const Params &p, int ntm, int ntn, int ntiles,
                                            volatile u32 *abort_flag, int pw, int lane) {
-  static_assert(Cfg::BN == 256, "one 16-byte chunk per lane covers a 256-column tile row");
+  constexpr int LPR = Cfg::BN / 8;  // lanes per tile row (16 bytes each)
+  constexpr int RPI = 32 / LPR;     // tile rows per warp instruction
+  static_assert(LPR * RPI == 32 && Cfg::BM % (4 * RPI * 8) == 0, "push layout");
   const unsigned short *out = static_cast<const unsigned short *>(p.out);
   const int ntasks = ntiles * p.npeer;
   const u32 need = 4u * p.epoch;
   for (int j = blockIdx.x; j < ntasks; j += gridDim.x) {
     const int t = j / p.npeer, g = j - t * p.npeer;
+    int tm, tn;
+    tile_coords<Cfg::GROUP_M>(t, ntm, ntn, tm, tn);
+    const u32 *flag = p.tile_flags + tm * ((p.GN + 63) / 64) + tn * (Cfg::BN / 64);
     int ok = 1;
     if (lane == 0) {
       const u64 t0 = globaltimer();
       for (;;) {
         u32 v;
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p.tile_flags + t) : "memory");
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
         if (static_cast<int>(v - need) >= 0) break;
         if (*abort_flag) { ok = 0; break; }
         if (globaltimer() - t0 > THORK_WAIT_TIMEOUT_NS) {
@@ -271,22 +276,21 @@ __device__ __forceinline__ void push_tasks(const Params &p, int ntm, int ntn, in
       }
     }
     if (!__shfl_sync(0xffffffffu, ok, 0)) break;
-    int tm, tn;
-    tile_coords<Cfg::GROUP_M>(t, ntm, ntn, tm, tn);
-    const int col = tn * Cfg::BN + lane * 8;
+    const int col = tn * Cfg::BN + (lane % LPR) * 8;
     // N is a multiple of 8, so a lane's 16-byte chunk is wholly in or out
     const int row_end = col < p.out_cols ? min(tm * Cfg::BM + Cfg::BM, p.out_rows) : 0;
     unsigned short *dst = nullptr;
 #pragma unroll
     for (int q = 0; q < 7; ++q)  // constant indices keep p.peer in parameter space
       if (q == g) dst = static_cast<unsigned short *>(p.peer[q]);
+    // warp pw takes row groups pw, pw + 4, ... of RPI consecutive rows
+    const int row_first = tm * Cfg::BM + pw * RPI + lane / LPR;
 #pragma unroll 1
-    for (int r0 = tm * Cfg::BM + pw; r0 < row_end; r0 += 32) {
-      // eight rows in flight: r0, r0+4, ..., r0+28 of this warp's share
-      uint4 v[8];
+    for (int r0 = row_first; r0 < tm * Cfg::BM + Cfg::BM; r0 += 32 * RPI) {
+      uint4 v[8];  // eight row groups in flight
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const int row = r0 + 4 * i;
+        const int row = r0 + 4 * RPI * i;
         if (row < row_end) {
           const unsigned short *src = out + static_cast<long long>(row) * p.ldo + col;
           asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
@@ -296,7 +300,7 @@ __device__ __forceinline__ void push_tasks(const Params &p, int ntm, int ntn, in
       }
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const int row = r0 + 4 * i;
+        const int row = r0 + 4 * RPI * i;
         if (row < row_end)
           st_global_v4(dst + static_cast<long long>(row) * p.ldo + col, v[i].x, v[i].y, v[i].z,
                        v[i].w);
@@ -487,7 +491,15 @@ __global__ void __launch_bounds__(gemm_threads<Cfg, AG>(), 1)
         // on the same flags mix the variants)
         if (lane == 0 && p.tile_flags) {
           __threadfence();
-          asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.tile_flags + t) : "memory");
+          // one count per 128 x 64 unit of C, whatever the tile width, so
+          // calls with different tile widths keep the same epochs
+          const int upr = (p.GN + 63) / 64;
+          const int u0 = tn * (Cfg::BN / 64);
+#pragma unroll
+          for (int u = 0; u < (Cfg::BN + 63) / 64; ++u)
+            if (u0 + u < upr)
+              asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.tile_flags + tm * upr + u0 + u)
+                           : "memory");
         }
       }
     }

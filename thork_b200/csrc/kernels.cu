@@ -248,8 +248,8 @@ using CfgSkinny256 = Config<KIND_BF16, 256, 4, true, false, true>;
 
 enum KernelId {
   K_GEMM_BF16 = 0, K_GEMM_E4M3, K_SKINNY16, K_SKINNY32, K_SKINNY64, K_SKINNY128, K_SKINNY256,
-  K_GEMM2_BF16, K_GEMM2_E4M3, K_SKSK16, K_SKSK32, K_GEMM_BF16_AG, K_GEMM_E4M3_AG,
-  K_GEMM_BF16_AGP, K_GEMM_E4M3_AGP
+  K_GEMM2_BF16, K_GEMM2_E4M3, K_SKSK16, K_SKSK32,
+  K_AG_BF16, K_AGP_BF16, K_AG_E4M3, K_AGP_E4M3  // fused all-gather: staged, push warps
 };
 
 template <class Cfg, int AG = AG_NONE>
@@ -362,10 +362,10 @@ namespace {
 // shared-memory staging tile); variant 2 leaves that to four push warps per
 // CTA that share all (tile, peer) pushes of the grid; 0 chooses.
 template <class Cfg>
-int gemm_allgather(int kid_staged, int kid_push, int dt, int elem, const void *d_a_rows,
-                   const void *d_b, void *d_c, void *const *d_peer_c, int n_peers, int rows, int N,
-                   int K, int row0, unsigned *d_tile_flags, unsigned epoch, float alpha,
-                   int variant, void *stream, const char *what) {
+int gemm_allgather(int kid_staged, int kid_push, int dt, int elem, const void *d_a_rows, const void *d_b, void *d_c,
+                   void *const *d_peer_c, int n_peers, int rows, int N, int K, int row0,
+                   unsigned *d_tile_flags, unsigned epoch, float alpha, int variant, void *stream,
+                   const char *what) {
   int rc;
   if ((rc = check_dims(rows, N, K, 16 / elem, what))) return rc;
   if ((rc = check_ptrs(d_a_rows, d_b, d_c, what))) return rc;
@@ -406,18 +406,18 @@ extern "C" int thork_gemm_bf16_allgather(const void *d_a_rows, const void *d_b, 
                                         void *const *d_peer_c, int n_peers, int rows, int N, int K,
                                         int row0, unsigned *d_tile_flags, unsigned epoch,
                                         int variant, void *stream) {
-  return gemm_allgather<CfgBf16>(K_GEMM_BF16_AG, K_GEMM_BF16_AGP, THORK_DT_BF16, 2, d_a_rows, d_b,
-                                 d_c, d_peer_c, n_peers, rows, N, K, row0, d_tile_flags, epoch,
-                                 1.0f, variant, stream, "gemm_bf16_allgather");
+  return gemm_allgather<CfgBf16>(
+      K_AG_BF16, K_AGP_BF16, THORK_DT_BF16, 2, d_a_rows, d_b, d_c, d_peer_c, n_peers, rows, N, K, row0,
+      d_tile_flags, epoch, 1.0f, variant, stream, "gemm_bf16_allgather");
 }
 
 extern "C" int thork_gemm_e4m3_allgather(const void *d_a_rows, const void *d_b, void *d_c,
                                         void *const *d_peer_c, int n_peers, int rows, int N, int K,
                                         int row0, unsigned *d_tile_flags, unsigned epoch,
                                         float scale_a, float scale_b, int variant, void *stream) {
-  return gemm_allgather<CfgE4m3>(K_GEMM_E4M3_AG, K_GEMM_E4M3_AGP, THORK_DT_E4M3, 1, d_a_rows, d_b,
-                                 d_c, d_peer_c, n_peers, rows, N, K, row0, d_tile_flags, epoch,
-                                 scale_a * scale_b, variant, stream, "gemm_e4m3_allgather");
+  return gemm_allgather<CfgE4m3>(
+      K_AG_E4M3, K_AGP_E4M3, THORK_DT_E4M3, 1, d_a_rows, d_b, d_c, d_peer_c, n_peers, rows, N, K, row0,
+      d_tile_flags, epoch, scale_a * scale_b, variant, stream, "gemm_e4m3_allgather");
 }
 
 namespace {

@@ -199,10 +199,11 @@ class FusedGather:
         self.peers = [q for q in range(self.world) if q != self.rank]
         self.epoch = 0
         self.calls = 0
-        # per-tile completion counts of the push-warp variant (this GPU only)
+        # completion counts per 128 x 64 unit of C for the push-warp
+        # variants (this GPU only)
         rows = max(e - s for s, e in (row_shard(self.m_total, self.world, q)
                                       for q in range(self.world)))
-        self.tile_flags = rt.DeviceArray((((rows + 127) // 128) * ((self.n + 255) // 256),),
+        self.tile_flags = rt.DeviceArray((((rows + 127) // 128) * ((self.n + 63) // 64),),
                                          np.uint32)
         self.tile_flags.zero()
         self.flag_ptrs = (ctypes.c_void_p * 8)(*[b + self.flag_off for b in self.peer_base])
