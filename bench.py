@@ -226,6 +226,15 @@ class GemmWorkload:
                                  scale=self.scale, gather=self.d.world > 1, stream=stream,
                                  gemm_done=ev1)
 
+    def local_step(self, stream, ev0=None, ev1=None):
+        """This rank's GEMM alone, without the all-gather (scaling reference)."""
+        if getattr(self, "C_loc", None) is None:
+            self.C_loc = self.rt.empty((self.m_loc, self.n), np.uint16)
+        if ev0 is not None:
+            ev0.record(stream)
+        self.dist.sharded_matmul(None, self.A, self.B, self.C_loc, self.m_loc, dtype=self.kind,
+                                 scale=self.scale, gather=False, stream=stream, gemm_done=ev1)
+
     def e2e_setup(self):
         rt = self.rt
         self.pa = rt.pinned_empty(self.a_host.shape, self.a_host.dtype)
@@ -523,6 +532,15 @@ def run_thork(args, d: Dist):
         "gpu_launches": args.steps * getattr(w, "launches_per_step", 1),
         "clocks": clocks,
     }
+    if isinstance(w, GemmWorkload) and d.world > 1:
+        # the same sharded GEMM without gathering C, for scaling with and without the gather
+        import types
+        loc_ms, _, _, _ = time_steps(types.SimpleNamespace(step=w.local_step), rt, args.steps,
+                                     args.warmup, d, per_launch_events=False)
+        loc_step = d.max(loc_ms / args.steps)
+        line["without_gather"] = {"value": round(w.flops_total / (loc_step * 1e-3) / 1e12, 2),
+                                  "unit": unit, "ms_per_step": round(loc_step, 5),
+                                  "gather_ms_per_step": round(ms_step - loc_step, 5)}
     if d.rank == 0 and d.world == 1:
         v, sample, _ = w.cpu_sample(args.cpu_seconds)
         line["cpu_baseline"] = {"value": round(v, 4), "unit": unit, "cores": os.cpu_count(),
