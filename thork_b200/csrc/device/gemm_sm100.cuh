@@ -746,31 +746,38 @@ __global__ void __launch_bounds__(192, 1)
         epi_bar();
         if (*last_flag) {
           __threadfence();
-          // sum the slots in slot order; all loads of a slot are in flight at once
+          // sum the slots in slot order, 32 columns at a time; all loads of a
+          // slot's chunk are in flight at once
           const float4 *slots = reinterpret_cast<const float4 *>(
               sp.partial + (static_cast<long long>(tile) * sp.max_seg * Cfg::BM + row) * Cfg::BN);
           constexpr int V = Cfg::BN / 4;
-          float4 sum[V];
+          constexpr int VC = V < 8 ? V : 8;
+#pragma unroll 1
+          for (int c = 0; c < V; c += VC) {
+            float4 sum[VC];
 #pragma unroll
-          for (int j = 0; j < V; ++j) sum[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int sgi = 0; sgi < nseg; ++sgi) {
-            float4 v[V];
+            for (int j = 0; j < VC; ++j) sum[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int sgi = 0; sgi < nseg; ++sgi) {
+              float4 v[VC];
 #pragma unroll
-            for (int j = 0; j < V; ++j) v[j] = __ldcg(slots + static_cast<long long>(sgi) * Cfg::BM * V + j);
+              for (int j = 0; j < VC; ++j)
+                v[j] = __ldcg(slots + static_cast<long long>(sgi) * Cfg::BM * V + c + j);
 #pragma unroll
-            for (int j = 0; j < V; ++j) {
-              sum[j].x += v[j].x;
-              sum[j].y += v[j].y;
-              sum[j].z += v[j].z;
-              sum[j].w += v[j].w;
+              for (int j = 0; j < VC; ++j) {
+                sum[j].x += v[j].x;
+                sum[j].y += v[j].y;
+                sum[j].z += v[j].z;
+                sum[j].w += v[j].w;
+              }
             }
-          }
-          if (n < p.out_cols) {
-            const float *f = reinterpret_cast<const float *>(sum);
+            if (n < p.out_cols) {
+              const float *f = reinterpret_cast<const float *>(sum);
 #pragma unroll
-            for (int m = 0; m < Cfg::BN; ++m)
-              if (m < p.out_rows)
-                st_global_b16(out + static_cast<long long>(m) * p.ldo + n, pack_bf16x2(f[m] * p.alpha, 0.0f));
+              for (int m = 0; m < 4 * VC; ++m)
+                if (4 * c + m < p.out_rows)
+                  st_global_b16(out + static_cast<long long>(4 * c + m) * p.ldo + n,
+                                pack_bf16x2(f[m] * p.alpha, 0.0f));
+            }
           }
           if (threadIdx.x == 64) sp.counters[tile] = 0u;  // ready for the next launch
         }

@@ -240,8 +240,11 @@ using Cfg2Bf16 = Config2<KIND_BF16, 256, 6>;
 using Cfg2E4m3 = Config2<KIND_E4M3, 256, 6>;
 // skinny (swap-AB): A = W row-major [K,N] (MN-major), B = X row-major [M,K]
 // (K-major), output written transposed into Y[M,N].
-using CfgSkinny16 = Config<KIND_BF16, 16, 10, true, false, true>;
-using CfgSkinny32 = Config<KIND_BF16, 32, 10, true, false, true>;
+// stream-K decode (M <= 32): 6 stages keep W streaming at the HBM rate and
+// leave room for the next launch's CTAs to start their prologue on the same
+// SM (measured: 3-10 stages within 2 %, M=32 11 % faster than with 10)
+using CfgSkinny16 = Config<KIND_BF16, 16, 6, true, false, true>;
+using CfgSkinny32 = Config<KIND_BF16, 32, 6, true, false, true>;
 using CfgSkinny64 = Config<KIND_BF16, 64, 8, true, false, true>;
 using CfgSkinny128 = Config<KIND_BF16, 128, 6, true, false, true>;
 using CfgSkinny256 = Config<KIND_BF16, 256, 4, true, false, true>;
