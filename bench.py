@@ -242,7 +242,9 @@ class GemmWorkload:
         self.pb = rt.pinned_empty(self.b_host.shape, self.b_host.dtype)
         self.pb[...] = self.b_host
         self.pc = rt.pinned_empty((self.m_loc, self.n), np.uint16)
-        self.h2d = self.pa.nbytes + self.pb.nbytes
+        # at N > 1 each rank copies its 1/N of B's rows; NVLink completes B
+        b_share = self.pb.nbytes // self.d.world if self.k % self.d.world == 0 else self.pb.nbytes
+        self.h2d = self.pa.nbytes + b_share
         self.d2h = self.pc.nbytes
 
     def e2e_step(self, tk):

@@ -327,10 +327,17 @@ def sharded_matmul(comm: Optional[Communicator], a_local: "rt.DeviceArray", b: "
 
 
 class _HostStaging:
-    """Device buffers reused across ``sharded_matmul_host`` calls."""
+    """Device buffers (and a side stream) reused across
+    ``sharded_matmul_host`` calls."""
 
     def __init__(self):
         self.bufs = {}
+        self._side = None
+
+    def side(self):
+        if self._side is None:
+            self._side = (rt.Stream(), rt.Event())
+        return self._side
 
     def get(self, key, shape, dtype):
         b = self.bufs.get(key)
@@ -343,20 +350,46 @@ class _HostStaging:
 _staging = _HostStaging()
 
 
+def replicate_host_rows(comm: Optional[Communicator], host: np.ndarray, dev: "rt.DeviceArray",
+                        stream: rt.Stream) -> int:
+    """Put the full row-major ``host`` array into ``dev`` on every rank while
+    each rank copies only its contiguous ``1/world`` of the rows over PCIe;
+    NCCL's in-place all-gather over NVLink supplies the rest.  Falls back to
+    a full copy when the rows do not split evenly.  Returns the bytes this
+    rank copied from the host."""
+    host = np.ascontiguousarray(host)
+    world = comm.world if comm is not None else 1
+    rows = host.shape[0]
+    if world == 1 or rows % world:
+        rt.copy_htod(dev.ptr, host, stream, sync=False)
+        return host.nbytes
+    start, stop = row_shard(rows, world, comm.rank)
+    row_bytes = host.nbytes // rows
+    rt.copy_htod(dev.ptr + start * row_bytes, host[start:stop], stream, sync=False)
+    count = (stop - start) * row_bytes
+    comm.allgather(dev.ptr + start * row_bytes, dev.ptr, count, 0, stream)  # bytes (uint8)
+    return count
+
+
 def sharded_matmul_host(comm: Optional[Communicator], a_rows: np.ndarray, b: np.ndarray,
                         c_rows: np.ndarray, m_total: int, *, dtype: str = "bf16",
                         scale: float = 1.0, fused: Optional[FusedGather] = None) -> None:
-    """Host-array form of ``sharded_matmul``: copies this rank's A rows and B
-    to the device, computes and all-gathers C on the devices (through
-    ``fused`` when given, else NCCL), and copies this rank's rows of C back
-    into ``c_rows``.  Synchronous."""
+    """Host-array form of ``sharded_matmul``: copies this rank's A rows and
+    its share of B's rows to the device (B is completed over NVLink by
+    ``replicate_host_rows``), computes and all-gathers C on the devices
+    (through ``fused`` when given, else NCCL), and copies this rank's rows of
+    C back into ``c_rows``.  Synchronous."""
     stream = rt._dispatch_stream()
     a_dev = _staging.get("a", a_rows.shape, a_rows.dtype)
     b_dev = _staging.get("b", b.shape, b.dtype)
     world = comm.world if comm is not None else 1
     if fused is not None and world > 1:
+        # B's NVLink all-gather runs on a side stream while A's rows cross PCIe
+        side, ev = _staging.side()
+        replicate_host_rows(comm, b, b_dev, side)
+        ev.record(side)
         rt.copy_htod(a_dev.ptr, np.ascontiguousarray(a_rows), stream, sync=False)
-        rt.copy_htod(b_dev.ptr, np.ascontiguousarray(b), stream, sync=False)
+        stream.wait(ev)
         c = fused.matmul(a_dev, b_dev, stream, dtype=dtype, scale_a=scale)
         start, _ = row_shard(m_total, world, comm.rank)
         rt.copy_dtoh(c_rows, c.ptr + start * b.shape[1] * 2, stream, sync=False)
@@ -364,8 +397,8 @@ def sharded_matmul_host(comm: Optional[Communicator], a_rows: np.ndarray, b: np.
         return
     rows_out = m_total if world > 1 else a_rows.shape[0]
     c_dev = _staging.get("c", (rows_out, b.shape[1]), np.uint16)
+    replicate_host_rows(comm, b, b_dev, stream)
     rt.copy_htod(a_dev.ptr, np.ascontiguousarray(a_rows), stream, sync=False)
-    rt.copy_htod(b_dev.ptr, np.ascontiguousarray(b), stream, sync=False)
     sharded_matmul(comm, a_dev, b_dev, c_dev, m_total, dtype=dtype, scale=scale,
                    gather=world > 1, stream=stream)
     rank = comm.rank if comm is not None else 0
