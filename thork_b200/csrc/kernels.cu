@@ -250,7 +250,7 @@ using CfgSkinny128 = Config<KIND_BF16, 128, 6, true, false, true>;
 using CfgSkinny256 = Config<KIND_BF16, 256, 4, true, false, true>;
 
 enum KernelId {
-  K_GEMM_BF16 = 0, K_GEMM_E4M3, K_SKINNY16, K_SKINNY32, K_SKINNY64, K_SKINNY128, K_SKINNY256,
+  K_GEMM_BF16 = 0, K_GEMM_E4M3, K_SKINNY64, K_SKINNY128, K_SKINNY256,
   K_GEMM2_BF16, K_GEMM2_E4M3, K_SKSK16, K_SKSK32,
   K_AG_BF16, K_AGP_BF16, K_AG_E4M3, K_AGP_E4M3  // fused all-gather: staged, push warps
 };
