@@ -433,8 +433,13 @@ struct PeerFlagPtrs {
   unsigned *p[8];
 };
 
+// Launched with programmatic stream serialisation: the block is resident
+// while the GEMM before it runs and starts signalling the moment that grid
+// completes, and the next launch may begin its prologue meanwhile.
 __global__ void peer_barrier_kernel(const PeerFlagPtrs peers, unsigned *flags, int world, int rank,
                                     unsigned epoch, unsigned *status) {
+  thork::dev::pdl_launch_dependents();
+  thork::dev::pdl_wait();  // the previous grid's stores are complete and visible from here on
   const int t = threadIdx.x;
   if (t < world && t != rank) {
     __threadfence_system();
@@ -475,9 +480,9 @@ extern "C" int thork_peer_barrier(void *d_flags, void *const *d_peer_flags, int 
   unsigned *status;
   int rc;
   if ((rc = thork_status_word(&status))) return rc;
-  peer_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
-      peers, static_cast<unsigned *>(d_flags), world, rank, epoch, status);
-  return launch_check("peer_barrier launch");
+  return launch_pdl(peer_barrier_kernel, dim3(1), 32, 0, static_cast<cudaStream_t>(stream), 1, false,
+                    "peer_barrier launch", peers, static_cast<unsigned *>(d_flags), world, rank,
+                    epoch, status);
 }
 
 namespace {
