@@ -8,7 +8,8 @@ unique-id broadcast) — the measured path is thork_b200 + libthork_rt.so.
 
 Workloads (default ``bf16_gemm_8192``):
   bf16_gemm_8192  C = A.B, 8192^3 bf16, A split by contiguous rows over the N
-                  GPUs, B replicated, C all-gathered with NCCL (strong scaling)
+                  GPUs, B replicated, C all-gathered inside the GEMM over NVLink
+                  (``--gather nccl``: NCCL all-gather after it); strong scaling
   bf16_gemm_4096  4096^3 bf16 (1 GPU config; rows split the same way at N > 1)
   e4m3_gemm_8192  8192^3 FP8 e4m3 with per-tensor scales, bf16 out, gathered
   skinny_m{1,16,128}  Y = X.W, K=4096, N=14336, bf16; W split by columns
