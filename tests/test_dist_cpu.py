@@ -106,3 +106,62 @@ def test_two_rank_gloo_shard_and_gather():
         p.join(timeout=120)
     results = dict(q.get(timeout=5) for _ in range(2))
     assert results == {0: "ok", 1: "ok"}
+
+
+class _HostComm:
+    """An in-place all-gather over host memory for ranks run as threads."""
+
+    def __init__(self, rank, world, shared):
+        self.rank, self.world, self.shared = rank, world, shared
+
+    def allgather(self, send_ptr, recv_ptr, count, dtype, stream=None):
+        import ctypes
+        self.shared["send"][self.rank] = send_ptr
+        self.shared["barrier"].wait()
+        for r in range(self.world):
+            if r != self.rank:
+                ctypes.memmove(recv_ptr + r * count, self.shared["send"][r], count)
+        self.shared["barrier"].wait()
+
+
+@pytest.mark.parametrize("rows,world", [(64, 4), (62, 4), (8, 1)])
+def test_replicate_host_rows_copies_one_share_per_rank(monkeypatch, rows, world):
+    """Each rank copies only its contiguous share of the rows and the
+    in-place all-gather completes the array on every rank; rows that do not
+    split evenly fall back to a full copy."""
+    import ctypes
+    import threading
+    from types import SimpleNamespace
+    copied = []  # bytes of every host copy (list.append is atomic)
+
+    def fake_htod(ptr, arr, stream=None, sync=True):
+        arr = np.ascontiguousarray(arr)
+        ctypes.memmove(ptr, arr.ctypes.data, arr.nbytes)
+        copied.append(arr.nbytes)
+
+    monkeypatch.setattr(dist.rt, "copy_htod", fake_htod)
+    host = np.random.default_rng(1).integers(0, 65535, (rows, 24), dtype=np.uint16)
+    devs = [np.zeros_like(host) for _ in range(world)]
+    shared = {"send": {}, "barrier": threading.Barrier(world)}
+    results, errors = [None] * world, []
+
+    def run(r):
+        try:
+            comm = _HostComm(r, world, shared) if world > 1 else None
+            dev = SimpleNamespace(ptr=devs[r].ctypes.data)
+            results[r] = dist.replicate_host_rows(comm, host, dev, None)
+        except Exception as exc:  # noqa: BLE001 - reported below
+            errors.append(exc)
+            shared["barrier"].abort()
+
+    threads = [threading.Thread(target=run, args=(r,)) for r in range(world)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=30)
+    assert not errors, errors
+    for d in devs:
+        np.testing.assert_array_equal(d, host)
+    share = host.nbytes // world if rows % world == 0 else host.nbytes
+    assert results == [share] * world
+    assert copied == [share] * world  # one copy per rank, of its share
