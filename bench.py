@@ -594,7 +594,99 @@ def also_measurements(args, d, rt, dist_mod, peaks):
     us = e0.elapsed_ms(e1) / 200 * 1e3
     out["add_f32_1024x1024"] = {"GB/s": round(12 * (1 << 20) / us / 1e3, 1), "us": round(us, 2),
                                 "note": "L2-resident, launch-latency bound"}
+    # the same config through the drop-in call with NumPy arrays (copy-in, launch, copy-back)
+    import thork_b200 as tk
+    ah = np.random.default_rng(0).standard_normal((1024, 1024), dtype=np.float32)
+    bh = np.random.default_rng(1).standard_normal((1024, 1024), dtype=np.float32)
+    ch = np.empty_like(ah)
+    add = tk.kernels.matrix_add((1024, 1024))
+    for _ in range(5):
+        add(ch, ah, bh)
+    t0 = time.perf_counter()
+    for _ in range(50):
+        add(ch, ah, bh)
+    call_us = (time.perf_counter() - t0) / 50 * 1e6
+    out["add_f32_1024x1024_dropin"] = {"us_per_call": round(call_us, 1),
+                                       "note": "kernel(out, a, b) on pageable NumPy arrays"}
+    out["traced_tile_gemm_4096"] = traced_tile_gemm(tk, rt, peaks)
     return out
+
+
+def traced_tile_gemm(tk, rt, peaks, size=4096):
+    """A user-written @tk.jit tile matmul in the style of the reference's
+    level-06 tcgen05 test kernel (one 128x128 output tile per CTA, a
+    single-stage TMA -> tcgen05.mma loop, TMEM -> registers -> shared -> TMA
+    store), timed device-resident: the traced tile path, not the library
+    GEMM."""
+    G = tk.kittens.Global
+    bf = tk.dt.bfloat16
+    TM, TN, TK = 128, 128, 64
+
+    @tk.jit
+    def tile_mm(A: G[bf, (TM, TK)], B: G[bf, (TK, TN)], D: G[bf, (TM, TN)], K: tk.Uint,
+                N: tk.Uint, bid: tk.Uint[tk.BlockIdx], tid: tk.Uint[tk.ThreadIdx]):
+        lane = tk.kittens.warpgroup.laneid()
+        bm = bid // (N // TN)
+        bn = bid % (N // TN)
+        a_s = tk.kittens.st_bf(TM, TK)
+        b_s = tk.kittens.st_bf(TK, TN)
+        d_s = tk.kittens.st_bf(TM, TN)
+        arrived = tk.kittens.semaphore()
+        consumed = tk.kittens.semaphore()
+        done = tk.kittens.semaphore()
+        with tk.if_(tid == 0):
+            tk.kittens.init_semaphore(arrived, 0, 1)
+            tk.kittens.init_semaphore(consumed, 1, 0)
+            tk.kittens.init_semaphore(done, 0, 1)
+        tk.syncthreads()
+        alloc = tk.kittens.tensor_allocator()
+        acc = tk.kittens.tt_fl(TM, TN)
+        with tk.if_(lane == 0):
+            tk.kittens.tensor_alloc(acc, alloc, 0)
+        tk.kittens.warpgroup.sync(1)
+        phase = tk.local(tk.dt.int32, 0)
+        for it in tk.range(K // TK):
+            with tk.if_(tid == 0):
+                tk.kittens.wait(consumed, phase ^ 1)
+                tk.kittens.tma.expect_bytes(arrived, (TM * TK + TK * TN) * 2)
+                tk.kittens.tma.load_async(a_s, A, (bm, it), arrived)
+                tk.kittens.tma.load_async(b_s, B, (it, bn), arrived)
+            tk.kittens.wait(arrived, phase)
+            phase ^= 1
+            with tk.if_(lane == 0):
+                with tk.if_(it == 0) as first:
+                    tk.kittens.warpgroup.mm_AB(acc, a_s, b_s, consumed)
+                with first.else_():
+                    tk.kittens.warpgroup.mma_AB(acc, a_s, b_s, consumed)
+        with tk.if_(lane == 0):
+            tk.kittens.tcgen05_commit(done)
+        tk.kittens.wait(done, 0)
+        d_r = tk.kittens.rt_bf(TM // 4, TN)
+        tk.kittens.warpgroup.load_async(d_r, acc)
+        tk.kittens.tensor_load_wait()
+        tk.kittens.warpgroup.sync(1)
+        tk.kittens.warpgroup.store(d_s, d_r)
+        tk.kittens.warpgroup.sync(1)
+        with tk.if_(lane == 0):
+            tk.kittens.tma.store_async(D, d_s, (bm, bn))
+            tk.kittens.tma.store_async_read_wait()
+
+    m = n = k = size
+    rng = np.random.default_rng(0)
+    A = rt.to_device(bf16_bits(rng.standard_normal((m, k), dtype=np.float32)))
+    B = rt.to_device(bf16_bits(rng.standard_normal((k, n), dtype=np.float32)))
+    D = rt.empty((m, n), np.uint16)
+    launch = tile_mm[((m // TM) * (n // TN), 1, 1), (128, 1, 1)]
+    launch(A, B, D, k, n)  # trace + NVRTC compile
+    reps = 20
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        launch(A, B, D, k, n)
+    ms = (time.perf_counter() - t0) / reps * 1e3  # launches are synchronous
+    tf = 2.0 * m * n * k / (ms * 1e-3) / 1e12
+    return {"TFLOP/s": round(tf, 1), "ms": round(ms, 4),
+            "frac_of_peak": round(tf / peaks["bf16_tflops"], 3),
+            "note": "user-style traced kernel; each launch synchronises like the reference's"}
 
 
 def traffic_from_profiles(workload):
