@@ -13,3 +13,8 @@ int thork_encode_tmap_2d(void *out128, int dtype, const void *base, uint64_t row
 int thork_status_word(unsigned **d_status);
 // Cached multiprocessor count of the current device.
 int thork_sm_count(int *n);
+// Pipelined copies through pinned slots for pageable host memory (staging.cu).
+bool thork_is_pageable(const void *host_ptr);
+size_t thork_staged_min_bytes();
+int thork_staged_htod(void *d_dst, const void *h_src, size_t n, cudaStream_t s);
+int thork_staged_dtoh(void *h_dst, const void *d_src, size_t n, cudaStream_t s);

@@ -210,6 +210,15 @@ static int do_copy(void *dst, const void *src, size_t n, cudaMemcpyKind kind, vo
   if (n == 0) return THORK_OK;
   if (!dst || !src) return thork_set_error(THORK_ERR_INVALID, "%s: NULL pointer", what);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // large copies to or from pageable memory take the pipelined pinned ring
+  if (n >= thork_staged_min_bytes() && kind != cudaMemcpyDeviceToDevice &&
+      thork_is_pageable(kind == cudaMemcpyHostToDevice ? src : dst)) {
+    int rc = kind == cudaMemcpyHostToDevice ? thork_staged_htod(dst, src, n, s)
+                                            : thork_staged_dtoh(dst, src, n, s);
+    if (rc == THORK_OK && sync && kind == cudaMemcpyHostToDevice)
+      CUDA_TRY(cudaStreamSynchronize(s), what);
+    return rc;
+  }
   if (sync && !s) {
     CUDA_TRY(cudaMemcpy(dst, src, n, kind), what);
   } else {
