@@ -106,6 +106,41 @@ def test_gemm_e4m3_config3_8192():
     assert err <= TOL, f"max rel err {err:.3e}"
 
 
+@pytest.mark.parametrize("variant", ["auto", "gemm2"])
+def test_gemm_bf16_config2_8192(variant):
+    """The headline config at full size: a 64-row sample of C against the
+    NumPy fp32 product of the bf16-rounded inputs, plus C(2A) == 2 C(A)."""
+    m = n = k = 8192
+    a16, b16 = _bf16_case(m, n, k, seed=0)
+    mm = tk.kernels.matmul(m, n, k, tk.dt.bfloat16, variant=variant)
+    c16 = np.zeros((m, n), np.uint16)
+    mm(c16, a16, b16)
+    rows = np.random.default_rng(1).choice(m, 64, replace=False)
+    ref = oracle.gemm_bf16_ref(a16[rows], b16)
+    err = oracle.max_rel_err(oracle.bf16_bits_to_f32(c16[rows]), ref)
+    assert err <= TOL, f"max rel err {err:.3e}"
+    a2 = oracle.f32_to_bf16_bits(oracle.bf16_bits_to_f32(a16) * 2)
+    c2 = np.zeros((m, n), np.uint16)
+    mm(c2, a2, b16)
+    np.testing.assert_array_equal(oracle.bf16_bits_to_f32(c2), 2 * oracle.bf16_bits_to_f32(c16))
+
+
+@pytest.mark.parametrize("m", [1, 16, 32, 128])
+def test_skinny_gemm_full_size_linear(m):
+    """Decode shapes at full size: Y(2X) == 2 Y(X) bit for bit (powers of two
+    commute with bf16 rounding and fp32 sums), and repeated calls agree."""
+    n, k = 14336, 4096
+    x, w = oracle.skinny_inputs(m, n, k, seed=7)
+    x16, w16 = oracle.f32_to_bf16_bits(x), oracle.f32_to_bf16_bits(w)
+    mm = tk.kernels.matmul(m, n, k, tk.dt.bfloat16, variant="skinny")
+    y1, y2, y3 = (np.zeros((m, n), np.uint16) for _ in range(3))
+    mm(y1, x16, w16)
+    mm(y2, x16, w16)
+    mm(y3, oracle.f32_to_bf16_bits(oracle.bf16_bits_to_f32(x16) * 2), w16)
+    np.testing.assert_array_equal(y1, y2)
+    np.testing.assert_array_equal(oracle.bf16_bits_to_f32(y3), 2 * oracle.bf16_bits_to_f32(y1))
+
+
 @pytest.mark.parametrize("m", [1, 16, 128, 5, 33, 200])
 def test_skinny_gemm_bf16(m):
     n, k = (14336, 4096) if m in (1, 16, 128) else (2048, 1024)
