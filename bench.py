@@ -321,8 +321,9 @@ class SkinnyWorkload:
         self.i += 1
         if ev0 is not None:
             ev0.record(stream)
-        self.rt.check(self.rt.lib().thork_skinny_gemm_bf16(
-            self.X.ptr, w.ptr, self.Y.ptr, self.m, self.n_loc, self.k, stream.handle))
+        # decode weights: no earlier kernel writes W (THORK_SKINNY_W_STATIC)
+        self.rt.check(self.rt.lib().thork_skinny_gemm_bf16_ex(
+            self.X.ptr, w.ptr, self.Y.ptr, self.m, self.n_loc, self.k, 1, stream.handle))
         if ev1 is not None:
             ev1.record(stream)
 
@@ -337,8 +338,8 @@ class SkinnyWorkload:
         self.d2h = self.py.nbytes
 
     def e2e_step(self, tk):
-        tk.kernels.matmul(self.m, self.n_loc, self.k, tk.dt.bfloat16, variant="skinny")(
-            self.py, self.px, self.pw)
+        tk.kernels.matmul(self.m, self.n_loc, self.k, tk.dt.bfloat16, variant="skinny",
+                          static_weights=True)(self.py, self.px, self.pw)
 
     def cpu_sample(self, seconds):
         from oracle import oracle

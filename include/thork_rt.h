@@ -255,6 +255,16 @@ THORK_API int thork_ipc_handle(const void *d_ptr, void *handle64);
 THORK_API int thork_ipc_open(const void *handle64, void **d_ptr);
 THORK_API int thork_ipc_close(void *d_ptr);
 
+/* thork_skinny_gemm_bf16 with flags.  THORK_SKINNY_W_STATIC promises that
+ * no kernel launched earlier on the stream writes W (decode weights): the
+ * stream-K kernel (M <= 32) then fetches W for its opening pipeline stages
+ * before its programmatic-dependent-launch wait, overlapping the previous
+ * kernel's tail.  X and Y keep the full stream ordering.  Larger M ignores
+ * the flag.  No reference counterpart.                                     */
+#define THORK_SKINNY_W_STATIC 1
+THORK_API int thork_skinny_gemm_bf16_ex(const void *d_x, const void *d_w, void *d_y, int M, int N,
+                                        int K, int flags, void *stream);
+
 /* Allocation-free form of thork_skinny_gemm_bf16 for 1 <= M <= 32 (the
  * stream-K decode path).  No reference counterpart: it exists for callers
  * that must not allocate device memory, directly or through this library --

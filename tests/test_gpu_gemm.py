@@ -212,3 +212,31 @@ def test_skinny_stream_k_repeated_calls_are_identical():
     assert all(np.array_equal(outs[0], o) for o in outs[1:])
     err = oracle.max_rel_err(oracle.bf16_bits_to_f32(outs[0]), oracle.gemm_bf16_ref(x16, w16))
     assert err <= TOL
+
+
+def test_skinny_static_weights_keep_the_activation_dependency():
+    """Two decode GEMMs chained on one stream, the second reading the first's
+    output as its X, with THORK_SKINNY_W_STATIC on both: W is fetched early,
+    X still waits for the previous kernel.  Bit-equal to the chain without
+    the flag, and within tolerance of the oracle on the same inputs."""
+    rt = tk.runtime
+    L = rt.lib()
+    m, k1, n1, n2 = 16, 512, 1024, 2048
+    x, w1 = oracle.skinny_inputs(m, n1, k1, seed=11)
+    _, w2 = oracle.skinny_inputs(m, n2, n1, seed=12)
+    x16, w1_16, w2_16 = (oracle.f32_to_bf16_bits(v) for v in (x, w1, w2))
+    X, W1, W2 = rt.to_device(x16), rt.to_device(w1_16), rt.to_device(w2_16)
+    s = rt.Stream()
+    outs = {}
+    for flags in (0, 1):
+        Y1, Y2 = rt.empty((m, n1), np.uint16), rt.empty((m, n2), np.uint16)
+        for _ in range(3):  # back to back, so the dependent launches overlap
+            rt.check(L.thork_skinny_gemm_bf16_ex(X.ptr, W1.ptr, Y1.ptr, m, n1, k1, flags, s.handle))
+            rt.check(L.thork_skinny_gemm_bf16_ex(Y1.ptr, W2.ptr, Y2.ptr, m, n2, n1, flags, s.handle))
+        s.synchronize()
+        outs[flags] = (Y1.to_host(), Y2.to_host())
+    assert rt.kernel_status() == 0
+    np.testing.assert_array_equal(outs[1][0], outs[0][0])
+    np.testing.assert_array_equal(outs[1][1], outs[0][1])
+    ref = oracle.gemm_bf16_ref(outs[0][0], w2_16)
+    assert oracle.max_rel_err(oracle.bf16_bits_to_f32(outs[1][1]), ref) <= TOL

@@ -529,6 +529,7 @@ struct SkParams {
   unsigned *counters;   // [tiles], zero between launches
   int base, extra;      // CTA c owns base + (c < extra) units
   int max_seg;          // slots per tile in `partial`
+  int w_static;         // W is written by no earlier launch: prefetch it before the dependency wait
 };
 
 __device__ __forceinline__ int sk_first_unit(int c, int base, int extra) {
@@ -622,23 +623,42 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const u32 tmem_base = *tmem_slot;
-  pdl_wait();  // the previous kernel of the stream is complete from here on
+  // the previous kernel of the stream is complete from pdl_wait() on; the
+  // producer may first fetch W for its opening stages when W is static
+  if (warp != 0) pdl_wait();
 
   if (warp == 0) {
     if (lane == 0) {
+      // Static W: the opening STAGES stages get their W tiles while the
+      // previous kernel still runs; X follows after the dependency wait.
+      int npre = 0;
+      if (sp.w_static) {
+        int u = u_begin, tile, k0, k1;
+        while (npre < Cfg::STAGES && sk_next(u, u_end, nkb, tile, k0, k1)) {
+          for (int kb = k0; kb < k1 && npre < Cfg::STAGES; ++kb, ++npre) {
+            const u32 sa = stage0 + npre * Cfg::STAGE_BYTES;
+            mbar_arrive_expect_tx(full_bar(npre), Cfg::STAGE_BYTES);
+            load_operand<Cfg>(sa, &tmap_a, full_bar(npre), true, Cfg::BM, tile * Cfg::BM, kb * Cfg::BK);
+          }
+        }
+      }
+      pdl_wait();
       int s = 0;
       u32 ph = 0;
+      int issued = 0;
       int u = u_begin, tile, k0, k1;
       while (!*abort_flag && sk_next(u, u_end, nkb, tile, k0, k1)) {
-        for (int kb = k0; kb < k1; ++kb) {
-          if (!mbar_wait(empty_bar(s), ph ^ 1u, p.status, 0x21)) {
-            *abort_flag = 1;
-            break;
-          }
+        for (int kb = k0; kb < k1; ++kb, ++issued) {
           const u32 sa = stage0 + s * Cfg::STAGE_BYTES;
           const u32 sb = sa + Cfg::A_BYTES;
-          mbar_arrive_expect_tx(full_bar(s), Cfg::STAGE_BYTES);
-          load_operand<Cfg>(sa, &tmap_a, full_bar(s), true, Cfg::BM, tile * Cfg::BM, kb * Cfg::BK);
+          if (issued >= npre) {
+            if (!mbar_wait(empty_bar(s), ph ^ 1u, p.status, 0x21)) {
+              *abort_flag = 1;
+              break;
+            }
+            mbar_arrive_expect_tx(full_bar(s), Cfg::STAGE_BYTES);
+            load_operand<Cfg>(sa, &tmap_a, full_bar(s), true, Cfg::BM, tile * Cfg::BM, kb * Cfg::BK);
+          }
           load_operand<Cfg>(sb, &tmap_b, full_bar(s), false, Cfg::BN, 0, kb * Cfg::BK);
           if (++s == Cfg::STAGES) {
             s = 0;

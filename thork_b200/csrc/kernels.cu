@@ -558,7 +558,8 @@ int sk_workspace(size_t partial_bytes, size_t counter_bytes, void **partial, voi
 
 template <class Cfg>
 int launch_skinny_sk(int kernel_id, const TensorMap &ta, const TensorMap &tb, const Params &prm,
-                     const SkPlan &pl, void *partial, void *counters, cudaStream_t s) {
+                     const SkPlan &pl, void *partial, void *counters, cudaStream_t s,
+                     bool w_static = false) {
   int rc;
   auto kern = skinny_sk_kernel<Cfg>;
   if ((rc = ensure_smem(reinterpret_cast<const void *>(kern), kernel_id, Cfg::SMEM_BYTES))) return rc;
@@ -569,6 +570,7 @@ int launch_skinny_sk(int kernel_id, const TensorMap &ta, const TensorMap &tb, co
   sp.base = pl.base;
   sp.extra = pl.extra;
   sp.max_seg = pl.max_seg;
+  sp.w_static = w_static ? 1 : 0;
   return launch_pdl(kern, dim3(pl.grid), Cfg::THREADS, Cfg::SMEM_BYTES, s, 1, false, "skinny_sk_kernel launch",
                     ta, tb, sp);
 }
@@ -585,7 +587,7 @@ int encode_skinny_maps(TensorMap &ta, TensorMap &tb, const void *d_x, const void
 
 template <class Cfg>
 int run_skinny_sk(int kernel_id, const void *d_x, const void *d_w, void *d_y, int M, int N, int K,
-                  cudaStream_t s) {
+                  cudaStream_t s, bool w_static) {
   int rc, sms;
   alignas(64) TensorMap ta, tb;
   if ((rc = encode_skinny_maps<Cfg>(ta, tb, d_x, d_w, M, N, K))) return rc;
@@ -596,7 +598,7 @@ int run_skinny_sk(int kernel_id, const void *d_x, const void *d_w, void *d_y, in
   unsigned *status;
   if ((rc = thork_status_word(&status))) return rc;
   Params prm{d_y, N, M, K, N, M, N, 1.0f, status};
-  return launch_skinny_sk<Cfg>(kernel_id, ta, tb, prm, pl, part, cnt, s);
+  return launch_skinny_sk<Cfg>(kernel_id, ta, tb, prm, pl, part, cnt, s, w_static);
 }
 
 template <class Cfg>
@@ -617,20 +619,28 @@ int run_skinny(int kernel_id, const void *d_x, const void *d_w, void *d_y, int M
 }
 }  // namespace
 
-extern "C" int thork_skinny_gemm_bf16(const void *d_x, const void *d_w, void *d_y, int M, int N,
-                                      int K, void *stream) {
+extern "C" int thork_skinny_gemm_bf16_ex(const void *d_x, const void *d_w, void *d_y, int M, int N,
+                                         int K, int flags, void *stream) {
   int rc;
   if ((rc = check_dims(M, N, K, 8, "skinny_gemm_bf16"))) return rc;
   if ((rc = check_ptrs(d_x, d_w, d_y, "skinny_gemm_bf16"))) return rc;
+  if (flags & ~THORK_SKINNY_W_STATIC)
+    return thork_set_error(THORK_ERR_INVALID, "skinny_gemm_bf16: unknown flags 0x%x", flags);
+  const bool w_static = (flags & THORK_SKINNY_W_STATIC) != 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // M <= 32: stream-K over all SMs (partials are small); larger M: one CTA
   // per 128-column tile
-  if (M <= 16) return run_skinny_sk<CfgSkinny16>(K_SKSK16, d_x, d_w, d_y, M, N, K, s);
-  if (M <= 32) return run_skinny_sk<CfgSkinny32>(K_SKSK32, d_x, d_w, d_y, M, N, K, s);
+  if (M <= 16) return run_skinny_sk<CfgSkinny16>(K_SKSK16, d_x, d_w, d_y, M, N, K, s, w_static);
+  if (M <= 32) return run_skinny_sk<CfgSkinny32>(K_SKSK32, d_x, d_w, d_y, M, N, K, s, w_static);
   if (M <= 64) return run_skinny<CfgSkinny64>(K_SKINNY64, d_x, d_w, d_y, M, N, K, s);
   if (M <= 128) return run_skinny<CfgSkinny128>(K_SKINNY128, d_x, d_w, d_y, M, N, K, s);
   if (M <= 256) return run_skinny<CfgSkinny256>(K_SKINNY256, d_x, d_w, d_y, M, N, K, s);
   return thork_set_error(THORK_ERR_INVALID, "skinny_gemm_bf16: M must be <= 256 (M=%d)", M);
+}
+
+extern "C" int thork_skinny_gemm_bf16(const void *d_x, const void *d_w, void *d_y, int M, int N,
+                                      int K, void *stream) {
+  return thork_skinny_gemm_bf16_ex(d_x, d_w, d_y, M, N, K, 0, stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -90,12 +90,15 @@ class _GemmKernel(LibraryKernel):
         super().__call__(*args, stream=stream, sync=sync)
 
 
-def matmul(M: int, N: int, K: int, dtype: dt.Dtype = dt.float32, variant: str = "auto"):
+def matmul(M: int, N: int, K: int, dtype: dt.Dtype = dt.float32, variant: str = "auto",
+           static_weights: bool = False):
     """Return a kernel ``k(out, A, B)`` for ``out[M,N] = A[M,K] @ B[K,N]``.
 
     ``variant``: ``"auto"``, ``"gemm"`` (128x256 tcgen05 tiles, one CTA),
     ``"gemm2"`` (256x256 tiles on a 2-CTA cluster) or, bf16 only,
-    ``"skinny"`` (swap-AB, M <= 256).
+    ``"skinny"`` (swap-AB, M <= 256).  ``static_weights`` (skinny): B is
+    written by no earlier kernel on the stream (decode weights), so the
+    kernel may start fetching it before the previous kernel has finished.
     """
     M, N, K = int(M), int(N), int(K)
     if dtype == dt.float32:
@@ -113,8 +116,10 @@ def matmul(M: int, N: int, K: int, dtype: dt.Dtype = dt.float32, variant: str = 
             if M > 256:
                 raise ValueError(f"matmul(bf16, skinny): M must be <= 256, got {M}")
 
+            flags = 1 if static_weights else 0  # THORK_SKINNY_W_STATIC
+
             def launch(p, s):
-                return rt.lib().thork_skinny_gemm_bf16(p[1], p[2], p[0], M, N, K, s)
+                return rt.lib().thork_skinny_gemm_bf16_ex(p[1], p[2], p[0], M, N, K, flags, s)
 
             name = "skinny_gemm_bf16"
         elif variant in ("gemm", "gemm2", "gemm_auto"):

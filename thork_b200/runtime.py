@@ -91,6 +91,7 @@ _SIGNATURES = {
     "thork_gemm_e4m3": [_vp, _vp, _vp, _i, _i, _i, ctypes.c_float, ctypes.c_float, _i, _vp],
     "thork_skinny_gemm_bf16": [_vp, _vp, _vp, _i, _i, _i, _vp],
     "thork_skinny_gemm_bf16_noalloc": [_vp, _vp, _vp, _i, _i, _i, _vp],
+    "thork_skinny_gemm_bf16_ex": [_vp, _vp, _vp, _i, _i, _i, _i, _vp],
     "thork_gemm_bf16_allgather": [_vp, _vp, _vp, _pvp, _i, _i, _i, _i, _i, _vp, ctypes.c_uint, _i,
                                   _vp],
     "thork_gemm_e4m3_allgather": [_vp, _vp, _vp, _pvp, _i, _i, _i, _i, _i, _vp, ctypes.c_uint,
