@@ -214,14 +214,15 @@ def test_skinny_stream_k_repeated_calls_are_identical():
     assert err <= TOL
 
 
-def test_skinny_static_weights_keep_the_activation_dependency():
+@pytest.mark.parametrize("m", [16, 128])
+def test_skinny_static_weights_keep_the_activation_dependency(m):
     """Two decode GEMMs chained on one stream, the second reading the first's
     output as its X, with THORK_SKINNY_W_STATIC on both: W is fetched early,
     X still waits for the previous kernel.  Bit-equal to the chain without
     the flag, and within tolerance of the oracle on the same inputs."""
     rt = tk.runtime
     L = rt.lib()
-    m, k1, n1, n2 = 16, 512, 1024, 2048
+    k1, n1, n2 = 512, 1024, 2048
     x, w1 = oracle.skinny_inputs(m, n1, k1, seed=11)
     _, w2 = oracle.skinny_inputs(m, n2, n1, seed=12)
     x16, w1_16, w2_16 = (oracle.f32_to_bf16_bits(v) for v in (x, w1, w2))
