@@ -442,19 +442,25 @@ def describe(name, w, world):
             "l2_policy": "3 GiB of traffic per step (> L2)"}, "GB/s", "hbm"
 
 
-def time_steps(w, rt, steps, warmup, d, per_launch_events=True):
+def time_steps(w, rt, steps, warmup, d, per_launch_events=True, sample_every=10):
+    """Time ``steps`` back-to-back steps with CUDA events around the whole
+    run; the dominant kernel's launch duration comes from events around every
+    ``sample_every``-th launch inside the same run (an event between two
+    launches stops the second from starting early, so not every launch is
+    bracketed)."""
     s = rt.Stream()
     for _ in range(warmup):
         w.step(s)
     s.synchronize()
-    evs = [(rt.Event(), rt.Event()) for _ in range(steps)] if per_launch_events else None
+    sampled = list(range(0, steps, sample_every)) if per_launch_events else []
+    evs = {i: (rt.Event(), rt.Event()) for i in sampled}
     e0, e1 = rt.Event(), rt.Event()
     rt.synchronize()
     d.barrier()
     t_wall0 = time.perf_counter()
     e0.record(s)
     for i in range(steps):
-        if evs:
+        if i in evs:
             w.step(s, evs[i][0], evs[i][1])
         else:
             w.step(s)
@@ -462,7 +468,7 @@ def time_steps(w, rt, steps, warmup, d, per_launch_events=True):
     e1.synchronize()
     t_wall1 = time.perf_counter()
     total_ms = e0.elapsed_ms(e1)
-    kernel_ms = (sum(a.elapsed_ms(b) for a, b in evs) / steps) if evs else total_ms / steps
+    kernel_ms = (sum(a.elapsed_ms(b) for a, b in evs.values()) / len(evs)) if evs else total_ms / steps
     rt.synchronize()
     d.barrier()
     return total_ms, kernel_ms, t_wall0, t_wall1
