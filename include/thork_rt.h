@@ -192,7 +192,10 @@ THORK_API int thork_matrix_add_f32(float *d_out, const float *d_a, const float *
 
 /* C[M,N] = A[M,K] . B[K,N], bf16 in, fp32 accumulate (tcgen05, TMEM),
  * bf16 out.  Requires K % 8 == 0 and N % 8 == 0 (16-byte TMA strides).
- * `variant` 0 = automatic, 1 = 1-CTA 128x256 tiles, 2 = 2-CTA 256x256.
+ * `variant` 0 = automatic, 1 = 1-CTA 128x256 tiles, 2 = 2-CTA 256x256,
+ * 3 = stream-K over 128x256 tiles (whole waves one tile per CTA, the tiles
+ * of the last wave split into equal k-loop shares over all SMs; chosen
+ * automatically when the tiles fill at most half of the SMs).
  * Replaces tk.kernels.matmul (src/thork/kernels/matmul.py:17-71, fp32 SIMT
  * only) for dtype=bfloat16, and the level-06 tcgen05 matmul that
  * tests/test_kittens.py:187-274 can only compile.                          */
@@ -201,6 +204,7 @@ THORK_API int thork_gemm_bf16(const void *d_a, const void *d_b, void *d_c,
 
 /* C[M,N] = (scale_a*scale_b) * (A[M,K] . B[K,N]) with A, B float8 e4m3
  * (bytes), fp32 accumulate, bf16 out.  Requires K % 16 == 0, N % 16 == 0.
+ * Variants as for thork_gemm_bf16 (0 = 2-CTA above M=128, else 1-CTA).
  * No reference counterpart (the reference has no FP8 dtype,
  * src/thork/dtypes.py:18-36); it is tk.kernels.matmul(dtype=float8_e4m3). */
 THORK_API int thork_gemm_e4m3(const void *d_a, const void *d_b, void *d_c,
@@ -280,8 +284,8 @@ THORK_API int thork_skinny_gemm_bf16_ex(const void *d_x, const void *d_w, void *
  *   - The scratch is shared by every call and keeps the last call's contents:
  *     each call clears the parts that must start at zero, and calls that can
  *     overlap on the GPU (different streams, other threads) race on it.
- *   - Limits: M <= 32, ceil(N/128) <= 16384 output tiles, and the split-tile
- *     partials of the problem must fit the array; larger requests return
+ *   - Limits: M <= 32 and ceil(N/128) <= 16384 output tiles (the split-tile
+ *     partials, two slots per CTA, always fit); larger requests return
  *     THORK_ERR_INVALID with the sizes in the message.  Inputs, output and
  *     stream are as for thork_skinny_gemm_bf16; no cudaMalloc, cudaFree or
  *     other allocating call is made.                                       */

@@ -106,6 +106,41 @@ def test_gemm_e4m3_config3_8192():
     assert err <= TOL, f"max rel err {err:.3e}"
 
 
+@pytest.mark.parametrize("m,n,k", [(4096, 4096, 4096), (1000, 784, 1296), (128, 256, 8192),
+                                   (300, 4112, 64), (2176, 2560, 512)])
+@pytest.mark.parametrize("dtype", ["bf16", "e4m3"])
+def test_gemm_stream_k(m, n, k, dtype):
+    """Stream-K (equal k-loop shares per SM, split tiles summed in a fixup):
+    ragged shapes, a K-only-deep case where every tile is split, a K=64
+    case where every CTA holds whole tiles, and the 4096^3 config."""
+    a, b = oracle.gemm_inputs(m, n, k, seed=9)
+    c16 = np.zeros((m, n), np.uint16)
+    if dtype == "bf16":
+        a16, b16 = oracle.f32_to_bf16_bits(a), oracle.f32_to_bf16_bits(b)
+        tk.kernels.matmul(m, n, k, tk.dt.bfloat16, variant="gemm_sk")(c16, a16, b16)
+        ref = oracle.gemm_bf16_ref(a16, b16)
+    else:
+        qa, sa = oracle.quantize_e4m3(a)
+        qb, sb = oracle.quantize_e4m3(b)
+        tk.kernels.matmul(m, n, k, tk.dt.float8_e4m3, variant="gemm_sk")(c16, qa, qb, sa, sb)
+        ref = oracle.gemm_e4m3_ref(qa, sa, qb, sb)
+    err = oracle.max_rel_err(oracle.bf16_bits_to_f32(c16), ref)
+    assert err <= TOL, f"max rel err {err:.3e}"
+    assert tk.runtime.kernel_status() == 0
+
+
+def test_gemm_stream_k_is_deterministic_and_linear():
+    m, n, k = 1000, 776, 1288
+    a16, b16 = _bf16_case(m, n, k, seed=13)
+    mm = tk.kernels.matmul(m, n, k, tk.dt.bfloat16, variant="gemm_sk")
+    c1, c2, c3 = (np.zeros((m, n), np.uint16) for _ in range(3))
+    mm(c1, a16, b16)
+    mm(c2, a16, b16)
+    mm(c3, oracle.f32_to_bf16_bits(oracle.bf16_bits_to_f32(a16) * 2), b16)
+    np.testing.assert_array_equal(c1, c2)
+    np.testing.assert_array_equal(oracle.bf16_bits_to_f32(c3), 2 * oracle.bf16_bits_to_f32(c1))
+
+
 @pytest.mark.parametrize("variant", ["auto", "gemm2"])
 def test_gemm_bf16_config2_8192(variant):
     """The headline config at full size: a 64-row sample of C against the

@@ -54,7 +54,8 @@ def test_no_alloc_entry_point_rejects_oversized_requests():
     assert lib.thork_skinny_gemm_bf16_noalloc(dummy.ptr, dummy.ptr, dummy.ptr, 33, 1024, 512, None) \
         == rt.ERR_INVALID
     assert "M must be <= 32" in rt.last_error()
-    # 32 rows x 1M columns x 8192 deep: split-tile partials exceed the array
-    assert lib.thork_skinny_gemm_bf16_noalloc(dummy.ptr, dummy.ptr, dummy.ptr, 32, 1 << 20, 8192, None) \
-        == rt.ERR_INVALID
+    # more than 16384 output tiles of 128 columns: the tile counters exceed the array
+    # (rejected on the host before anything is launched)
+    assert lib.thork_skinny_gemm_bf16_noalloc(dummy.ptr, dummy.ptr, dummy.ptr, 32, 16385 * 128, 512,
+                                              None) == rt.ERR_INVALID
     assert "scratch array" in rt.last_error()

@@ -525,12 +525,20 @@ __global__ void __launch_bounds__(gemm_threads<Cfg, AG>(), 1)
 // ===========================================================================
 struct SkParams {
   Params p;
-  float *partial;       // [tiles][max_seg][BM][BN] fp32
+  float *partial;       // [grid][2][BN/4][BM] float4: a CTA's first and last segment
   unsigned *counters;   // [tiles], zero between launches
-  int base, extra;      // CTA c owns base + (c < extra) units
-  int max_seg;          // slots per tile in `partial`
-  int w_static;         // W is written by no earlier launch: prefetch it before the dependency wait
+  int base, extra;      // CTA c owns base + (c < extra) stream-K units
+  int dp_tiles;         // leading tiles done whole, CTA c taking c, c + grid, ...
+  int w_static;         // A is written by no earlier launch: prefetch it before the dependency wait
 };
+
+
+
+// A CTA's unit range is contiguous, so only its first and last segments can
+// be part of a tile; slot 0 holds the first, slot 1 the last.
+__device__ __forceinline__ int sk_slot(int c, int tile, int nkb, int base, int extra) {
+  return (c * base + min(c, extra)) / nkb == tile ? 0 : 1;
+}
 
 __device__ __forceinline__ int sk_first_unit(int c, int base, int extra) {
   return c * base + min(c, extra);
@@ -551,6 +559,25 @@ __device__ __forceinline__ bool sk_next(int &u, int end, int nkb, int &tile, int
   u = e;
   return true;
 }
+
+// The CTA's work in order: its whole data-parallel tiles, then the
+// segments of its stream-K unit range (units count from tile dp_tiles on).
+struct SkIter {
+  int t_dp, u;
+  __device__ __forceinline__ bool next(const SkParams &sp, int u_end, int nkb, int &tile, int &k0,
+                                       int &k1) {
+    if (t_dp < sp.dp_tiles) {
+      tile = t_dp;
+      k0 = 0;
+      k1 = nkb;
+      t_dp += gridDim.x;
+      return true;
+    }
+    if (!sk_next(u, u_end, nkb, tile, k0, k1)) return false;
+    tile += sp.dp_tiles;
+    return true;
+  }
+};
 
 // Named barrier 1 over the 128 epilogue threads.
 __device__ __forceinline__ void epi_bar() {
@@ -574,10 +601,9 @@ __device__ __forceinline__ bool epi_vote_any(bool v) {
 
 template <class Cfg>
 __global__ void __launch_bounds__(192, 1)
-    skinny_sk_kernel(const __grid_constant__ TensorMap tmap_a, const __grid_constant__ TensorMap tmap_b,
-                     const SkParams sp) {
+    sk_kernel(const __grid_constant__ TensorMap tmap_a, const __grid_constant__ TensorMap tmap_b,
+              const SkParams sp) {
   pdl_launch_dependents();
-  static_assert(Cfg::A_MN && !Cfg::B_MN && Cfg::TRANS_OUT, "stream-K path is the swap-AB decode GEMM");
   const Params &p = sp.p;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const u32 raw = smem_u32(smem_raw);
@@ -597,6 +623,8 @@ __global__ void __launch_bounds__(192, 1)
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const int nkb = (p.GK + Cfg::BK - 1) / Cfg::BK;
+  const int ntm = (p.GM + Cfg::BM - 1) / Cfg::BM;
+  const int ntn = (p.GN + Cfg::BN - 1) / Cfg::BN;
   const int u_begin = sk_first_unit(blockIdx.x, sp.base, sp.extra);
   const int u_end = sk_first_unit(blockIdx.x + 1, sp.base, sp.extra);
 
@@ -633,12 +661,16 @@ __global__ void __launch_bounds__(192, 1)
       // previous kernel still runs; X follows after the dependency wait.
       int npre = 0;
       if (sp.w_static) {
-        int u = u_begin, tile, k0, k1;
-        while (npre < Cfg::STAGES && sk_next(u, u_end, nkb, tile, k0, k1)) {
+        SkIter pre{static_cast<int>(blockIdx.x), u_begin};
+        int tile, k0, k1;
+        while (npre < Cfg::STAGES && pre.next(sp, u_end, nkb, tile, k0, k1)) {
+          int tm, tn;
+          tile_coords<Cfg::GROUP_M>(tile, ntm, ntn, tm, tn);
           for (int kb = k0; kb < k1 && npre < Cfg::STAGES; ++kb, ++npre) {
             const u32 sa = stage0 + npre * Cfg::STAGE_BYTES;
             mbar_arrive_expect_tx(full_bar(npre), Cfg::STAGE_BYTES);
-            load_operand<Cfg>(sa, &tmap_a, full_bar(npre), true, Cfg::BM, tile * Cfg::BM, kb * Cfg::BK);
+            load_operand<Cfg>(sa, &tmap_a, full_bar(npre), Cfg::A_MN, Cfg::BM, tm * Cfg::BM,
+                              kb * Cfg::BK);
           }
         }
       }
@@ -646,8 +678,11 @@ __global__ void __launch_bounds__(192, 1)
       int s = 0;
       u32 ph = 0;
       int issued = 0;
-      int u = u_begin, tile, k0, k1;
-      while (!*abort_flag && sk_next(u, u_end, nkb, tile, k0, k1)) {
+      SkIter itr{static_cast<int>(blockIdx.x), u_begin};
+      int tile, k0, k1;
+      while (!*abort_flag && itr.next(sp, u_end, nkb, tile, k0, k1)) {
+        int tm, tn;
+        tile_coords<Cfg::GROUP_M>(tile, ntm, ntn, tm, tn);
         for (int kb = k0; kb < k1; ++kb, ++issued) {
           const u32 sa = stage0 + s * Cfg::STAGE_BYTES;
           const u32 sb = sa + Cfg::A_BYTES;
@@ -657,9 +692,9 @@ __global__ void __launch_bounds__(192, 1)
               break;
             }
             mbar_arrive_expect_tx(full_bar(s), Cfg::STAGE_BYTES);
-            load_operand<Cfg>(sa, &tmap_a, full_bar(s), true, Cfg::BM, tile * Cfg::BM, kb * Cfg::BK);
+            load_operand<Cfg>(sa, &tmap_a, full_bar(s), Cfg::A_MN, Cfg::BM, tm * Cfg::BM, kb * Cfg::BK);
           }
-          load_operand<Cfg>(sb, &tmap_b, full_bar(s), false, Cfg::BN, 0, kb * Cfg::BK);
+          load_operand<Cfg>(sb, &tmap_b, full_bar(s), Cfg::B_MN, Cfg::BN, tn * Cfg::BN, kb * Cfg::BK);
           if (++s == Cfg::STAGES) {
             s = 0;
             ph ^= 1u;
@@ -679,8 +714,9 @@ __global__ void __launch_bounds__(192, 1)
       int s = 0;
       u32 ph = 0;
       int it = 0;
-      int u = u_begin, tile, k0, k1;
-      while (!*abort_flag && sk_next(u, u_end, nkb, tile, k0, k1)) {
+      SkIter itr{static_cast<int>(blockIdx.x), u_begin};
+      int tile, k0, k1;
+      while (!*abort_flag && itr.next(sp, u_end, nkb, tile, k0, k1)) {
         const int acc = it & 1;
         const u32 acc_ph = (it >> 1) & 1;
         const u32 d_tmem = tmem_base + acc * Cfg::BN;
@@ -698,9 +734,14 @@ __global__ void __launch_bounds__(192, 1)
           const u32 sa = stage0 + s * Cfg::STAGE_BYTES;
           const u32 sb = sa + Cfg::A_BYTES;
 #pragma unroll
-          for (int k = 0; k < Cfg::BK / Cfg::UMMA_K; ++k)
-            mma_f16_ss(d_tmem, operand_desc<Cfg>(sa, true, k), operand_desc<Cfg>(sb, false, k), Cfg::IDESC,
-                       (kb > k0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < Cfg::BK / Cfg::UMMA_K; ++k) {
+            const u64 ad = operand_desc<Cfg>(sa, Cfg::A_MN, k), bd = operand_desc<Cfg>(sb, Cfg::B_MN, k);
+            const u32 accum = (kb > k0 || k > 0) ? 1u : 0u;
+            if constexpr (Cfg::KIND == KIND_BF16)
+              mma_f16_ss(d_tmem, ad, bd, Cfg::IDESC, accum);
+            else
+              mma_f8f6f4_ss(d_tmem, ad, bd, Cfg::IDESC, accum);
+          }
           tc_commit(empty_bar(s));
           if (++s == Cfg::STAGES) {
             s = 0;
@@ -717,11 +758,12 @@ __global__ void __launch_bounds__(192, 1)
     __syncwarp();
   } else {
     const int q = warp & 3;
-    const int row = q * 32 + lane;  // TMEM lane = output column (n) within the tile
+    const int row = q * 32 + lane;  // TMEM lane: MMA-space row within the tile
     unsigned short *out = static_cast<unsigned short *>(p.out);
     int it = 0;
-    int u = u_begin, tile, k0, k1;
-    while (sk_next(u, u_end, nkb, tile, k0, k1)) {
+    SkIter itr{static_cast<int>(blockIdx.x), u_begin};
+    int tile, k0, k1;
+    while (itr.next(sp, u_end, nkb, tile, k0, k1)) {
       const int acc = it & 1;
       const u32 acc_ph = (it >> 1) & 1;
       bool ok = true;
@@ -734,14 +776,21 @@ __global__ void __launch_bounds__(192, 1)
       }
       tc_fence_after();
       const u32 t_row = tmem_base + ((u32)(q * 32) << 16) + acc * Cfg::BN;
-      const int n = tile * Cfg::BM + row;
+      int tm, tn;
+      tile_coords<Cfg::GROUP_M>(tile, ntm, ntn, tm, tn);
+      // MMA-space row: the output column n (swap-AB) or the output row m
+      const int n = tm * Cfg::BM + row;
       if (k0 == 0 && k1 == nkb) {
-        bf16_store_tile<Cfg>(p, t_row, n, 0);
+        bf16_store_tile<Cfg>(p, t_row, n, tn * Cfg::BN);
       } else {
-        const int first = sk_cta_of_unit(tile * nkb, sp.base, sp.extra);
-        const int nseg = sk_cta_of_unit((tile + 1) * nkb - 1, sp.base, sp.extra) - first + 1;
-        const int slot = blockIdx.x - first;
-        float *mine = sp.partial + ((static_cast<long long>(tile) * sp.max_seg + slot) * Cfg::BM + row) * Cfg::BN;
+        const int lt = tile - sp.dp_tiles;  // tile index within the stream-K units
+        const int first = sk_cta_of_unit(lt * nkb, sp.base, sp.extra);
+        const int nseg = sk_cta_of_unit((lt + 1) * nkb - 1, sp.base, sp.extra) - first + 1;
+        const int slot = sk_slot(blockIdx.x, lt, nkb, sp.base, sp.extra);
+        // slot layout [BN/4][BM] float4: a warp's 32 rows of one 4-column
+        // chunk are 512 contiguous bytes, for both this write and the fixup
+        float4 *mine = reinterpret_cast<float4 *>(sp.partial) +
+                       (static_cast<long long>(blockIdx.x) * 2 + slot) * (Cfg::BN / 4) * Cfg::BM + row;
         constexpr int CH = (Cfg::BN % 32 == 0) ? 32 : 16;
 #pragma unroll 1
         for (int c0 = 0; c0 < Cfg::BN; c0 += CH) {
@@ -753,7 +802,7 @@ __global__ void __launch_bounds__(192, 1)
           tmem_wait_ld();
 #pragma unroll
           for (int j = 0; j < CH / 4; ++j)
-            *reinterpret_cast<float4 *>(mine + c0 + 4 * j) =
+            mine[(c0 / 4 + j) * Cfg::BM] =
                 make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
                             __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
         }
@@ -766,10 +815,8 @@ __global__ void __launch_bounds__(192, 1)
         epi_bar();
         if (*last_flag) {
           __threadfence();
-          // sum the slots in slot order, 32 columns at a time; all loads of a
-          // slot's chunk are in flight at once
-          const float4 *slots = reinterpret_cast<const float4 *>(
-              sp.partial + (static_cast<long long>(tile) * sp.max_seg * Cfg::BM + row) * Cfg::BN);
+          // sum the covering CTAs' slots in CTA order, 32 columns at a time;
+          // all loads of a slot's chunk are in flight at once
           constexpr int V = Cfg::BN / 4;
           constexpr int VC = V < 8 ? V : 8;
 #pragma unroll 1
@@ -778,10 +825,14 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
             for (int j = 0; j < VC; ++j) sum[j] = make_float4(0.f, 0.f, 0.f, 0.f);
             for (int sgi = 0; sgi < nseg; ++sgi) {
+              const int cta = first + sgi;
+              const float4 *slot4 =
+                  reinterpret_cast<const float4 *>(sp.partial) +
+                  (static_cast<long long>(cta) * 2 + sk_slot(cta, lt, nkb, sp.base, sp.extra)) * V * Cfg::BM +
+                  row;
               float4 v[VC];
 #pragma unroll
-              for (int j = 0; j < VC; ++j)
-                v[j] = __ldcg(slots + static_cast<long long>(sgi) * Cfg::BM * V + c + j);
+              for (int j = 0; j < VC; ++j) v[j] = __ldcg(slot4 + (c + j) * Cfg::BM);
 #pragma unroll
               for (int j = 0; j < VC; ++j) {
                 sum[j].x += v[j].x;
@@ -790,13 +841,28 @@ __global__ void __launch_bounds__(192, 1)
                 sum[j].w += v[j].w;
               }
             }
-            if (n < p.out_cols) {
-              const float *f = reinterpret_cast<const float *>(sum);
+            const float *f = reinterpret_cast<const float *>(sum);
+            if constexpr (Cfg::TRANS_OUT) {
+              if (n < p.out_cols) {
 #pragma unroll
-              for (int m = 0; m < 4 * VC; ++m)
-                if (4 * c + m < p.out_rows)
-                  st_global_b16(out + static_cast<long long>(4 * c + m) * p.ldo + n,
-                                pack_bf16x2(f[m] * p.alpha, 0.0f));
+                for (int m = 0; m < 4 * VC; ++m)
+                  if (4 * c + m < p.out_rows)
+                    st_global_b16(out + static_cast<long long>(4 * c + m) * p.ldo + n,
+                                  pack_bf16x2(f[m] * p.alpha, 0.0f));
+              }
+            } else if (n < p.out_rows) {
+              // row n of C, columns tn*BN + 4c .. + 4 VC, 16-byte stores
+#pragma unroll
+              for (int g = 0; g < VC / 2; ++g) {
+                const int col = tn * Cfg::BN + 4 * c + 8 * g;
+                if (col < p.out_cols) {
+                  u32 w[4];
+#pragma unroll
+                  for (int h = 0; h < 4; ++h)
+                    w[h] = pack_bf16x2(f[8 * g + 2 * h] * p.alpha, f[8 * g + 2 * h + 1] * p.alpha);
+                  st_global_v4(out + static_cast<long long>(n) * p.ldo + col, w[0], w[1], w[2], w[3]);
+                }
+              }
             }
           }
           if (threadIdx.x == 64) sp.counters[tile] = 0u;  // ready for the next launch

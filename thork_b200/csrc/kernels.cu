@@ -251,7 +251,7 @@ using CfgSkinny256 = Config<KIND_BF16, 256, 4, true, false, true>;
 
 enum KernelId {
   K_GEMM_BF16 = 0, K_GEMM_E4M3, K_SKINNY64, K_SKINNY128, K_SKINNY256,
-  K_GEMM2_BF16, K_GEMM2_E4M3, K_SKSK16, K_SKSK32,
+  K_GEMM2_BF16, K_GEMM2_E4M3, K_SKSK16, K_SKSK32, K_GEMM_BF16_SK, K_GEMM_E4M3_SK,
   K_AG_BF16, K_AGP_BF16, K_AG_E4M3, K_AGP_E4M3  // fused all-gather: staged, push warps
 };
 
@@ -285,6 +285,11 @@ int run_gemm2(int kernel_id, const TensorMap &ta, const TensorMap &tb, const Par
                     prm);
 }
 
+template <class Cfg>
+int run_gemm_sk(int kernel_id, const TensorMap &ta, const TensorMap &tb, const Params &prm,
+                cudaStream_t s);
+bool prefer_stream_k(long long tiles, int sms);
+
 int check_dims(int M, int N, int K, int align, const char *what) {
   if (M <= 0 || N <= 0 || K <= 0)
     return thork_set_error(THORK_ERR_INVALID, "%s: dimensions must be positive (M=%d N=%d K=%d)",
@@ -311,7 +316,7 @@ extern "C" int thork_gemm_bf16(const void *d_a, const void *d_b, void *d_c, int 
   int rc;
   if ((rc = check_dims(M, N, K, 8, "gemm_bf16"))) return rc;
   if ((rc = check_ptrs(d_a, d_b, d_c, "gemm_bf16"))) return rc;
-  if (variant < 0 || variant > 2)
+  if (variant < 0 || variant > 3)
     return thork_set_error(THORK_ERR_INVALID, "gemm_bf16: unknown variant %d", variant);
   alignas(64) TensorMap ta, tb;
   using C = CfgBf16;
@@ -325,9 +330,16 @@ extern "C" int thork_gemm_bf16(const void *d_a, const void *d_b, void *d_c, int 
   Params prm{d_c, M, N, K, N, M, N, 1.0f, status};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // automatic choice: under the power cap the 1-CTA kernel sustains ~3% more
-  // on bf16 (same-box A/B at 8192^3)
-  if (variant == 0) variant = 1;
+  // on bf16 than the 2-CTA one (same-box A/B at 8192^3); stream-K when the
+  // 128 x 256 tiles would fill at most half of the SMs
+  if (variant == 0) {
+    int sms;
+    if ((rc = thork_sm_count(&sms))) return rc;
+    const long long tiles = static_cast<long long>((M + C::BM - 1) / C::BM) * ((N + C::BN - 1) / C::BN);
+    variant = prefer_stream_k(tiles, sms) ? 3 : 1;
+  }
   if (variant == 2) return run_gemm2<Cfg2Bf16>(K_GEMM2_BF16, ta, tb, prm, s, "gemm2_bf16 launch");
+  if (variant == 3) return run_gemm_sk<C>(K_GEMM_BF16_SK, ta, tb, prm, s);
   return run_gemm<C>(K_GEMM_BF16, ta, tb, prm, s, "gemm_bf16 launch");
 }
 
@@ -336,7 +348,7 @@ extern "C" int thork_gemm_e4m3(const void *d_a, const void *d_b, void *d_c, int 
   int rc;
   if ((rc = check_dims(M, N, K, 16, "gemm_e4m3"))) return rc;
   if ((rc = check_ptrs(d_a, d_b, d_c, "gemm_e4m3"))) return rc;
-  if (variant < 0 || variant > 2)
+  if (variant < 0 || variant > 3)
     return thork_set_error(THORK_ERR_INVALID, "gemm_e4m3: unknown variant %d", variant);
   alignas(64) TensorMap ta, tb;
   using C = CfgE4m3;
@@ -352,6 +364,7 @@ extern "C" int thork_gemm_e4m3(const void *d_a, const void *d_b, void *d_c, int 
   // pair tile has work for both CTAs
   if (variant == 0) variant = (M > 128) ? 2 : 1;
   if (variant == 2) return run_gemm2<Cfg2E4m3>(K_GEMM2_E4M3, ta, tb, prm, s, "gemm2_e4m3 launch");
+  if (variant == 3) return run_gemm_sk<C>(K_GEMM_E4M3_SK, ta, tb, prm, s);
   return run_gemm<C>(K_GEMM_E4M3, ta, tb, prm, s, "gemm_e4m3 launch");
 }
 
@@ -486,37 +499,38 @@ extern "C" int thork_peer_barrier(void *d_flags, void *const *d_peer_flags, int 
 }
 
 namespace {
-// ---- stream-K decode GEMM -------------------------------------------------
+// ---- stream-K GEMM ----------------------------------------------------------
 struct SkPlan {
-  int grid, base, extra, tiles, max_seg;
+  int grid, base, extra, tiles, dp_tiles;
   size_t partial_bytes, counter_bytes;
 };
 
-int sk_cta_of_unit_host(int u, int base, int extra) {
-  const int big = extra * (base + 1);
-  return u < big ? u / (base + 1) : extra + (u - big) / base;
-}
-
-// Equal contiguous ranges of (tile, k-block) units over the SMs.
-SkPlan sk_plan(int M_pad_cols, int N, int K, int sms) {
+// Work split for a GEMM in MMA space GM x GN x GK.  With `data_parallel`,
+// the whole waves of tiles go one tile per CTA (in raster order, so the
+// tiles in flight share operand panels in L2) and only the tiles of the
+// last, partial wave are split into equal contiguous ranges of (tile,
+// k-block) units; otherwise every tile is.  Each CTA owns two partial slots.
+template <class Cfg>
+SkPlan sk_plan(int GM, int GN, int GK, int sms, bool data_parallel = false) {
   SkPlan pl;
-  const int BM = 128, BK = 64;
-  pl.tiles = (N + BM - 1) / BM;
-  const int nkb = (K + BK - 1) / BK;
-  const long long units = static_cast<long long>(pl.tiles) * nkb;
-  pl.grid = static_cast<int>(units < sms ? units : sms);
+  pl.tiles = ((GM + Cfg::BM - 1) / Cfg::BM) * ((GN + Cfg::BN - 1) / Cfg::BN);
+  const int nkb = (GK + Cfg::BK - 1) / Cfg::BK;
+  pl.dp_tiles = data_parallel && pl.tiles > sms ? (pl.tiles - 1) / sms * sms : 0;
+  const long long units = static_cast<long long>(pl.tiles - pl.dp_tiles) * nkb;
+  pl.grid = pl.dp_tiles ? sms : static_cast<int>(units < sms ? units : sms);
   pl.base = static_cast<int>(units / pl.grid);
   pl.extra = static_cast<int>(units % pl.grid);
-  pl.max_seg = 1;
-  for (int t = 0; t < pl.tiles; ++t) {
-    const int c0 = sk_cta_of_unit_host(t * nkb, pl.base, pl.extra);
-    const int c1 = sk_cta_of_unit_host((t + 1) * nkb - 1, pl.base, pl.extra);
-    if (c1 - c0 + 1 > pl.max_seg) pl.max_seg = c1 - c0 + 1;
-  }
-  pl.partial_bytes = static_cast<size_t>(pl.tiles) * pl.max_seg * BM * M_pad_cols * sizeof(float);
+  pl.partial_bytes = static_cast<size_t>(pl.grid) * 2 * Cfg::BM * Cfg::BN * sizeof(float);
   pl.counter_bytes = static_cast<size_t>(pl.tiles) * sizeof(unsigned);
   return pl;
 }
+
+// Stream-K splits the k-loop of the tiles over all SMs at the cost of a
+// partial write and a fixup per split tile.  Measured on B200, that only
+// pays when whole tiles would leave most SMs idle (4096^3, 3.46 waves:
+// stream-K 5 % slower than whole tiles); it is chosen automatically when
+// the tiles fill at most half of the SMs.
+bool prefer_stream_k(long long tiles, int sms) { return tiles * 2 <= sms; }
 
 // Per-device workspaces of the stream-K path: the partial slots, and the
 // per-tile arrival counters in a buffer of their own (zeroed when allocated
@@ -557,11 +571,11 @@ int sk_workspace(size_t partial_bytes, size_t counter_bytes, void **partial, voi
 }
 
 template <class Cfg>
-int launch_skinny_sk(int kernel_id, const TensorMap &ta, const TensorMap &tb, const Params &prm,
-                     const SkPlan &pl, void *partial, void *counters, cudaStream_t s,
-                     bool w_static = false) {
+int launch_sk(int kernel_id, const TensorMap &ta, const TensorMap &tb, const Params &prm,
+              const SkPlan &pl, void *partial, void *counters, cudaStream_t s,
+              bool w_static = false) {
   int rc;
-  auto kern = skinny_sk_kernel<Cfg>;
+  auto kern = sk_kernel<Cfg>;
   if ((rc = ensure_smem(reinterpret_cast<const void *>(kern), kernel_id, Cfg::SMEM_BYTES))) return rc;
   SkParams sp;
   sp.p = prm;
@@ -569,10 +583,22 @@ int launch_skinny_sk(int kernel_id, const TensorMap &ta, const TensorMap &tb, co
   sp.counters = static_cast<unsigned *>(counters);
   sp.base = pl.base;
   sp.extra = pl.extra;
-  sp.max_seg = pl.max_seg;
+  sp.dp_tiles = pl.dp_tiles;
   sp.w_static = w_static ? 1 : 0;
-  return launch_pdl(kern, dim3(pl.grid), Cfg::THREADS, Cfg::SMEM_BYTES, s, 1, false, "skinny_sk_kernel launch",
+  return launch_pdl(kern, dim3(pl.grid), Cfg::THREADS, Cfg::SMEM_BYTES, s, 1, false, "sk_kernel launch",
                     ta, tb, sp);
+}
+
+// Stream-K form of the 128 x 256-tile GEMM (A K-major, B MN-major).
+template <class Cfg>
+int run_gemm_sk(int kernel_id, const TensorMap &ta, const TensorMap &tb, const Params &prm,
+                cudaStream_t s) {
+  int rc, sms;
+  if ((rc = thork_sm_count(&sms))) return rc;
+  const SkPlan pl = sk_plan<Cfg>(prm.GM, prm.GN, prm.GK, sms, true);
+  void *part, *cnt;
+  if ((rc = sk_workspace(pl.partial_bytes, pl.counter_bytes, &part, &cnt))) return rc;
+  return launch_sk<Cfg>(kernel_id, ta, tb, prm, pl, part, cnt, s);
 }
 
 template <class Cfg>
@@ -592,13 +618,13 @@ int run_skinny_sk(int kernel_id, const void *d_x, const void *d_w, void *d_y, in
   alignas(64) TensorMap ta, tb;
   if ((rc = encode_skinny_maps<Cfg>(ta, tb, d_x, d_w, M, N, K))) return rc;
   if ((rc = thork_sm_count(&sms))) return rc;
-  const SkPlan pl = sk_plan(Cfg::BN, N, K, sms);
+  const SkPlan pl = sk_plan<Cfg>(N, M, K, sms);
   void *part, *cnt;
   if ((rc = sk_workspace(pl.partial_bytes, pl.counter_bytes, &part, &cnt))) return rc;
   unsigned *status;
   if ((rc = thork_status_word(&status))) return rc;
   Params prm{d_y, N, M, K, N, M, N, 1.0f, status};
-  return launch_skinny_sk<Cfg>(kernel_id, ta, tb, prm, pl, part, cnt, s, w_static);
+  return launch_sk<Cfg>(kernel_id, ta, tb, prm, pl, part, cnt, s, w_static);
 }
 
 template <class Cfg>
@@ -683,7 +709,7 @@ int run_skinny_noalloc(int kernel_id, const void *d_x, const void *d_w, void *d_
                        cudaStream_t s) {
   int rc, sms;
   if ((rc = thork_sm_count(&sms))) return rc;
-  const SkPlan pl = sk_plan(Cfg::BN, N, K, sms);
+  const SkPlan pl = sk_plan<Cfg>(N, M, K, sms);
   if (pl.partial_bytes > kNoAllocPartialBytes)
     return thork_set_error(THORK_ERR_INVALID,
                            "skinny_gemm_bf16_noalloc: M=%d N=%d K=%d needs %zu bytes of split-tile "
@@ -699,7 +725,7 @@ int run_skinny_noalloc(int kernel_id, const void *d_x, const void *d_w, void *d_
   alignas(64) TensorMap ta, tb;
   if ((rc = encode_skinny_maps<Cfg>(ta, tb, d_x, d_w, M, N, K))) return rc;
   Params prm{d_y, N, M, K, N, M, N, 1.0f, reinterpret_cast<unsigned *>(base)};
-  return launch_skinny_sk<Cfg>(kernel_id, ta, tb, prm, pl, partial, counters, s);
+  return launch_sk<Cfg>(kernel_id, ta, tb, prm, pl, partial, counters, s);
 }
 }  // namespace
 

@@ -95,8 +95,9 @@ def matmul(M: int, N: int, K: int, dtype: dt.Dtype = dt.float32, variant: str = 
     """Return a kernel ``k(out, A, B)`` for ``out[M,N] = A[M,K] @ B[K,N]``.
 
     ``variant``: ``"auto"``, ``"gemm"`` (128x256 tcgen05 tiles, one CTA),
-    ``"gemm2"`` (256x256 tiles on a 2-CTA cluster) or, bf16 only,
-    ``"skinny"`` (swap-AB, M <= 256).  ``static_weights`` (skinny): B is
+    ``"gemm2"`` (256x256 tiles on a 2-CTA cluster), ``"gemm_sk"`` (128x256
+    tiles, stream-K: equal shares of the k-loop per SM, split tiles summed
+    in a fixup) or, bf16 only, ``"skinny"`` (swap-AB, M <= 256).  ``static_weights`` (skinny): B is
     written by no earlier kernel on the stream (decode weights), so the
     kernel may start fetching it before the previous kernel has finished.
     """
@@ -122,8 +123,8 @@ def matmul(M: int, N: int, K: int, dtype: dt.Dtype = dt.float32, variant: str = 
                 return rt.lib().thork_skinny_gemm_bf16_ex(p[1], p[2], p[0], M, N, K, flags, s)
 
             name = "skinny_gemm_bf16"
-        elif variant in ("gemm", "gemm2", "gemm_auto"):
-            code = {"gemm_auto": 0, "gemm": 1, "gemm2": 2}[variant]
+        elif variant in ("gemm", "gemm2", "gemm_sk", "gemm_auto"):
+            code = {"gemm_auto": 0, "gemm": 1, "gemm2": 2, "gemm_sk": 3}[variant]
 
             def launch(p, s):
                 return rt.lib().thork_gemm_bf16(p[1], p[2], p[0], M, N, K, code, s)
@@ -142,7 +143,7 @@ def matmul(M: int, N: int, K: int, dtype: dt.Dtype = dt.float32, variant: str = 
         specs = [ArgSpec("out", dt.bfloat16, M * N, written=True, overwrites=True),
                  ArgSpec("A", dt.float8_e4m3, M * K), ArgSpec("B", dt.float8_e4m3, K * N)]
 
-        code = {"auto": 0, "gemm": 1, "gemm2": 2}.get(variant)
+        code = {"auto": 0, "gemm": 1, "gemm2": 2, "gemm_sk": 3}.get(variant)
         if code is None:
             raise ValueError(f"matmul: unknown variant {variant!r}")
 
