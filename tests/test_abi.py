@@ -5,10 +5,8 @@ import ctypes
 import os
 import re
 
-import numpy as np
 import pytest
 
-import thork_b200 as tk
 from thork_b200 import runtime as rt
 
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))

@@ -11,7 +11,7 @@ ThunderKittens types, and there is no generated host launcher
 """
 
 import math
-from typing import Dict, List, Optional, Tuple
+from typing import Dict, List, Tuple
 
 from . import ir
 
