@@ -758,6 +758,15 @@ def run_reference(args, d: Dist):
         sample = f"NumPy a+b over {n} fp32 (2^26 of the 2^28 elements) per step"
     cfg = {"workload": name, "parallelism": "host CPU (rank 0)",
            "threads": os.environ.get("OPENBLAS_NUM_THREADS", "all cores")}
+    # the same problem keys as this benchmark's own arm
+    if name in ("bf16_gemm_8192", "bf16_gemm_4096", "e4m3_gemm_8192"):
+        cfg.update({"M": size, "N": size, "K": size, "dtype_in": name.split("_")[0],
+                    "compute": "fp32 NumPy matmul of the rounded inputs"})
+    elif name.startswith("skinny_m"):
+        cfg.update({"M": m, "N": 14336, "K": 4096, "dtype_in": "bf16",
+                    "compute": "fp32 NumPy matmul of the rounded inputs"})
+    else:
+        cfg.update({"elements": 1 << 28, "dtype_in": "fp32", "compute": "NumPy a + b"})
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": unit,
         "n_gpus": d.world, "steps": args.steps, "warmup": args.warmup,
