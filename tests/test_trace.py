@@ -51,6 +51,23 @@ def test_zoo_kernels_compile_for_sm100a(name, zoo):
     assert len(cubin) > 1000
 
 
+@pytest.mark.parametrize("name", ["regtile_matmul", "tma_matmul", "tcgen05_matmul"])
+def test_tile_matmul_kernels_compile_for_sm100a(name):
+    """The traced tile matmuls (register tiles + mma.sync, TMA into shared
+    tiles, tcgen05 into TMEM) lower through the tile library and compile."""
+    import tile_kernels
+    k = getattr(tile_kernels, name)(tk)
+    cubin = rt.nvrtc_compile(k.cuda_source, source_map=k.source_map)
+    assert len(cubin) > 1000
+
+
+@pytest.mark.parametrize("name", ["copy_tile", "tma_copy"])
+def test_tile_copy_kernels_compile_for_sm100a(name):
+    k = kernel_zoo.build_tiles(tk)[name]
+    cubin = rt.nvrtc_compile(k.cuda_source, source_map=k.source_map)
+    assert len(cubin) > 1000
+
+
 def test_validation_errors_match_reference():
     with open(os.path.join(GOLDEN, "reference_validation.json")) as f:
         ref = json.load(f)
