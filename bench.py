@@ -6,7 +6,7 @@ For N > 1 launch one process per GPU with torch.distributed.run; torch is
 used here only for host-side plumbing (gloo barrier, max-over-ranks, NCCL
 unique-id broadcast) — the measured path is thork_b200 + libthork_rt.so.
 
-Workloads (default ``bf16_gemm_8192``):
+Workloads (the target configurations; default ``bf16_gemm_8192``):
   bf16_gemm_8192  C = A.B, 8192^3 bf16, A split by contiguous rows over the N
                   GPUs, B replicated, C all-gathered inside the GEMM over NVLink
                   (``--gather nccl``: NCCL all-gather after it); strong scaling
@@ -530,7 +530,7 @@ def run_thork(args, d: Dist):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": {"bf16_gemm_8192": "bf16", "bf16_gemm_4096": "bf16", "e4m3_gemm_8192": "e4m3"}.get(
             args.workload, "bf16" if args.workload.startswith("skinny") else "f32"),
-        "data": "synthetic: seeded N(0,1) inputs (BASELINE shapes/distributions), host-rounded",
+        "data": "synthetic: seeded N(0,1) inputs (target shapes and distributions), host-rounded",
         "config": cfg,
         "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": round(peak, 1),
                      "unit": unit.replace("TFLOP/s", "TFLOP/s"), "frac": round(achieved / peak, 4),
@@ -570,7 +570,7 @@ def run_thork(args, d: Dist):
 
 
 def also_measurements(args, d, rt, dist_mod, peaks):
-    """Short device-resident timings of the other BASELINE configs (1 GPU)."""
+    """Short device-resident timings of the other target configurations (1 GPU)."""
     out = {}
     for name, steps in (("e4m3_gemm_8192", 100), ("bf16_gemm_4096", 200), ("skinny_m1", 300),
                         ("skinny_m16", 300), ("skinny_m128", 300), ("add_f32", 100)):

@@ -1,7 +1,7 @@
 """GPU parity: tcgen05 GEMMs against the oracle (NumPy fp32 matmul of the
 identically rounded inputs, reference ``tests/test_kittens.py:20-36, 101``).
 
-Tolerance: max|C - R| / max|R| <= 1e-2 for bf16 and
+Tolerance (the target specification): max|C - R| / max|R| <= 1e-2 for bf16 and
 FP8 e4m3.  Observed errors are ~1e-3 (bf16 output rounding).
 """
 
