@@ -164,6 +164,22 @@ class _Emitter:
             raise TypeError(f"Unknown statement node: {type(s).__name__}")
 
 
+def format_stmts(stmts: List[ir.Stmt], indent: int = 4) -> Tuple[str, Dict[int, tuple]]:
+    """CUDA text of ``stmts`` indented by ``indent`` spaces, and a map from
+    0-indexed line within the text to the Python source location
+    (reference ``codegen.py:191-202``)."""
+    em = _Emitter()
+    em.stmts(list(stmts), 0)
+    pad = " " * indent
+    text = "\n".join(pad + line for line in em.lines)
+    return text, {line - 1: loc for line, loc in em.smap.items()}
+
+
+def format_stmt(stmt: ir.Stmt, indent: int = 4) -> Tuple[str, Dict[int, tuple]]:
+    """``format_stmts`` of a single statement (reference ``codegen.py:101``)."""
+    return format_stmts([stmt], indent)
+
+
 def _param_decl(p: ir.Param) -> str:
     if p.kind == "pointer":
         return f"{p.dtype.cuda} *{p.name}"

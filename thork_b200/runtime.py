@@ -566,6 +566,103 @@ def compile_source(source: str, *, source_map=None, extra_opts: Sequence[str] = 
                                 include_dirs=include_dirs))
 
 
+def _nvcc_path() -> str:
+    home = os.environ.get("CUDA_HOME") or os.environ.get("CUDA_PATH") or "/usr/local/cuda"
+    cand = os.path.join(home, "bin", "nvcc")
+    if os.path.exists(cand):
+        return cand
+    import shutil
+    found = shutil.which("nvcc")
+    if not found:
+        raise RuntimeError("nvcc not found (set CUDA_HOME)")
+    return found
+
+
+def nvcc_compile(source: str, *, source_map=None, extra_opts: Optional[Sequence[str]] = None,
+                 include_dirs: Optional[Sequence[str]] = None,
+                 defines: Optional[Sequence[str]] = None) -> bytes:
+    """nvcc -> sm_100a cubin, for sources that need headers NVRTC cannot
+    reach.  Raises ``RuntimeError("nvcc compile failed: ...")`` with the log
+    rewritten to Python source locations."""
+    import subprocess
+    import tempfile
+    with tempfile.TemporaryDirectory(prefix="thork_b200_") as tmp:
+        src = os.path.join(tmp, "kernel.cu")
+        out = os.path.join(tmp, "kernel.cubin")
+        with open(src, "w") as f:
+            f.write(source)
+        cmd = [_nvcc_path(), "--cubin", "-gencode", "arch=compute_100a,code=sm_100a", "-std=c++17",
+               "-lineinfo", "-I", os.path.join(PKG_DIR, "csrc", "device")]
+        for d in include_dirs or ():
+            cmd += ["-I", d]
+        for d in defines or ():
+            cmd.append(d if d.startswith("-D") else "-D" + d)
+        cmd += list(extra_opts or ()) + [src, "-o", out]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            log = (r.stdout + r.stderr).replace(src, "<thork kernel>")
+            raise RuntimeError(f"nvcc compile failed:\n{rewrite_compile_error(log, source_map)}")
+        with open(out, "rb") as f:
+            return f.read()
+
+
+def compile_source_with_nvcc(source: str, *, source_map=None,
+                             extra_opts: Optional[Sequence[str]] = None,
+                             include_dirs: Optional[Sequence[str]] = None,
+                             defines: Optional[Sequence[str]] = None) -> Module:
+    """nvcc -> cubin (sm_100a) -> loaded module (reference ``runtime.py:312-338``)."""
+    return Module(nvcc_compile(source, source_map=source_map, extra_opts=extra_opts,
+                               include_dirs=include_dirs, defines=defines))
+
+
+def compile_source_to_shared_lib(source: str, **kwargs):
+    """The reference builds ThunderKittens kernels into host shared libraries
+    with generated launchers (``runtime.py:341-371``).  Tile kernels here are
+    NVRTC cubins launched through ``thork_launch``, so there is no host
+    launcher to build."""
+    raise NotImplementedError(
+        "compile_source_to_shared_lib: tile kernels compile to NVRTC cubins here and launch "
+        "through thork_launch; use compile_source() or @tk.jit")
+
+
+def dispatch_tk(lib, kernel_name, params, user_args, grid_size, block_size, shared_mem_bytes,
+                stream=0):
+    """Reference ``runtime.py:534-612`` launches ThunderKittens kernels through
+    their generated host launcher; ``dispatch`` launches every kernel here."""
+    raise NotImplementedError(
+        "dispatch_tk: tile kernels launch through runtime.dispatch (no generated host launcher)")
+
+
+def kittens_include_dirs() -> List[str]:
+    """Include directories of the tile library the tile kernels compile
+    against (reference ``runtime.py:121-136`` returns ThunderKittens')."""
+    return [os.path.join(PKG_DIR, "csrc", "device")]
+
+
+def kittens_sm_define_for_cap(cap: str) -> str:
+    """Architecture define for a compute capability string such as
+    ``"100"`` or ``"100a"`` (reference ``runtime.py:139-154``), for code that
+    passes it on to its own builds; the tile library itself is sm_100a."""
+    digits = cap.rstrip("a")
+    major = int(digits[:-1]) if len(digits) > 2 else int(digits[0])
+    if major >= 12:
+        return "KITTENS_SM120"
+    if major >= 10:
+        return "KITTENS_SM100"
+    return "KITTENS_SM90" if major == 9 else "KITTENS_SM80"
+
+
+def kittens_sm_define() -> str:
+    return kittens_sm_define_for_cap(get_compute_capability())
+
+
+def set_max_dynamic_shared_size(func: int) -> None:
+    """Opt ``func`` into the device's dynamic shared memory budget minus the
+    1 KiB reserve (reference ``runtime.py:189-200``)."""
+    check(lib().thork_function_set_max_dynamic_smem(func, max_dynamic_shared_size()),
+          "set max dynamic shared size")
+
+
 def get_function(module: Module, name: str) -> int:
     return module.function(name)
 

@@ -30,6 +30,21 @@ from .types import DevicePointerSpec
 _PKG_DIR = os.path.dirname(os.path.abspath(__file__)) + os.sep
 
 
+_stype_hooks: dict = {}
+
+
+def register_stype_hooks(**hooks) -> None:
+    """Registration point for a verification side-car's type-combination
+    hooks (keys ``binop``, ``unary``, ``math``, ``scalar``, ``local_init``;
+    reference ``tracer.py:144-154``).  The hooks are kept; tracing does not
+    consult them, since the verifier they serve is not part of this
+    package."""
+    unknown = set(hooks) - {"binop", "unary", "math", "scalar", "local_init"}
+    if unknown:
+        raise TypeError(f"register_stype_hooks: unknown hook(s) {sorted(unknown)}")
+    _stype_hooks.update(hooks)
+
+
 def user_location():
     """(filename, line) of the innermost frame outside the thork_b200 package."""
     f = sys._getframe(1)
