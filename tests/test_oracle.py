@@ -79,3 +79,27 @@ def test_seeded_inputs_are_deterministic():
     x, w = oracle.skinny_inputs(2, n=64, k=32)
     assert w.shape == (32, 64) and x.shape == (2, 32)
     assert abs(float(w.std()) - 0.02) < 0.005
+
+
+def test_product_rounding_helpers_match_the_oracle():
+    """The package's own host-side converters (used to prepare bf16 / e4m3
+    inputs) give the same bytes as the oracle's restatement of the
+    reference's rounding, including ties, subnormals and saturation."""
+    from thork_b200 import dtypes
+    rng = np.random.default_rng(5)
+    x = np.concatenate([
+        rng.standard_normal(20000).astype(np.float32),
+        (rng.standard_normal(2000) * 1e-39).astype(np.float32),   # subnormals
+        np.array([0.0, -0.0, 1.0, -1.0, 3.0e38, -3.0e38, 1e-45], np.float32),
+        np.frombuffer(rng.integers(0, 2**32, 4000, dtype=np.uint32).astype(np.uint32).tobytes(),
+                      np.float32),
+    ])
+    x = x[np.isfinite(x)]
+    np.testing.assert_array_equal(dtypes.to_bf16_bits(x), oracle.f32_to_bf16_bits(x))
+    np.testing.assert_array_equal(dtypes.from_bf16_bits(oracle.f32_to_bf16_bits(x)),
+                                  oracle.bf16_bits_to_f32(oracle.f32_to_bf16_bits(x)))
+    y = rng.standard_normal((64, 96)).astype(np.float32) * 7.0
+    qp, sp = dtypes.quantize_e4m3(y)
+    qo, so = oracle.quantize_e4m3(y)
+    assert np.float32(sp) == np.float32(so)
+    np.testing.assert_array_equal(np.asarray(qp).view(np.uint8), np.asarray(qo).view(np.uint8))
