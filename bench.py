@@ -19,21 +19,48 @@ Workloads (the target configurations; default ``bf16_gemm_8192``):
 A step is one pass of the hot path over one batch of synthetic input
 already resident in HBM (``value``).  ``e2e`` repeats the step through the
 public API (``tk.kernels.*`` / ``thork_b200.dist``) from pinned host buffers,
-host<->device copies included.  ``--impl reference`` times the reference's
-own CPU path (its NumPy verification arithmetic, restated in oracle/) on a
-bounded sample of the same workload, rank 0 only.
+host<->device copies included.  After the timed regions every rank checks
+its result (``check``): a seeded row sample of the gathered C against the
+oracle (covering every rank's rows), and at N > 1 the whole gathered C bit
+for bit against the NCCL all-gather path; the run exits non-zero when a
+check fails.  ``--impl reference`` times the reference's own CPU path (its
+NumPy verification arithmetic, restated in oracle/) on a bounded sample of
+the same workload, rank 0 only, with every host core.
+
+oracle/ is imported only by the CPU legs (``cpu_baseline``, the reference
+arm) and by the post-timing check, never inside a timed GPU region.
 """
 
-import argparse
-import json
 import os
-import statistics
-import subprocess
 import sys
-import threading
-import time
 
-import numpy as np
+
+def _impl_from_argv(argv):
+    for i, a in enumerate(argv):
+        if a == "--impl" and i + 1 < len(argv):
+            return argv[i + 1]
+        if a.startswith("--impl="):
+            return a.split("=", 1)[1]
+    return "thork"
+
+
+# The CPU legs use every host core.  torch.distributed.run exports
+# OMP_NUM_THREADS=1, and OpenBLAS fixes its thread pool when NumPy loads, so
+# the reference arm (rank 0 alone does the work) sets the counts before the
+# import.  The thork arm's cpu_baseline runs at N = 1 only, without torchrun.
+if _impl_from_argv(sys.argv) == "reference":
+    for _v in ("OPENBLAS_NUM_THREADS", "OMP_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[_v] = str(os.cpu_count() or 1)
+
+import argparse  # noqa: E402
+import json  # noqa: E402
+import math  # noqa: E402
+import statistics  # noqa: E402
+import subprocess  # noqa: E402
+import threading  # noqa: E402
+import time  # noqa: E402
+
+import numpy as np  # noqa: E402
 
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
@@ -41,6 +68,39 @@ sys.path.insert(0, REPO)
 METRIC = "bf16/fp8 GEMM TFLOP/s & % peak at 8192³; elementwise HBM GB/s; 1–8 GPUs"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 L2_BYTES = 126 * (1 << 20)
+TOL = 1e-2  # max |C - R| / max |R| for the bf16 / e4m3 GEMMs (north_star)
+CHECK_ROWS = 64
+
+
+def blas_threads():
+    """(threads the BLAS pool uses now, library name), via threadpoolctl."""
+    try:
+        from threadpoolctl import threadpool_info
+        for info in threadpool_info():
+            if info.get("user_api") == "blas":
+                return int(info.get("num_threads", 0)), info.get("internal_api", "blas")
+    except Exception:  # pragma: no cover - threadpoolctl missing or failing
+        pass
+    return None, None
+
+
+class all_host_threads:
+    """Context: let the BLAS pool use every host core (undoes an inherited
+    OMP_NUM_THREADS=1), restoring the previous limit on exit."""
+
+    def __enter__(self):
+        self._ctl = None
+        try:
+            from threadpoolctl import threadpool_limits
+            self._ctl = threadpool_limits(limits=os.cpu_count() or 1, user_api="blas")
+        except Exception:  # pragma: no cover
+            self._ctl = None
+        return self
+
+    def __exit__(self, *exc):
+        if self._ctl is not None:
+            self._ctl.restore_original_limits()
+        return False
 
 
 # --------------------------------------------------------------------------
@@ -51,24 +111,27 @@ class Dist:
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-        self.pg = None
         if self.world > 1:
             import datetime
             import torch.distributed as tdist
-            tdist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+            tdist.init_process_group("gloo", timeout=datetime.timedelta(seconds=180))
             self.tdist = tdist
 
     def barrier(self):
         if self.world > 1:
             self.tdist.barrier()
 
-    def max(self, x: float) -> float:
-        if self.world == 1:
-            return x
+    def _reduce(self, x: float, op) -> float:
         import torch
         t = torch.tensor([x], dtype=torch.float64)
-        self.tdist.all_reduce(t, op=self.tdist.ReduceOp.MAX)
+        self.tdist.all_reduce(t, op=op)
         return float(t.item())
+
+    def max(self, x: float) -> float:
+        return x if self.world == 1 else self._reduce(x, self.tdist.ReduceOp.MAX)
+
+    def min(self, x: float) -> float:
+        return x if self.world == 1 else self._reduce(x, self.tdist.ReduceOp.MIN)
 
     def bcast_bytes(self, b):
         if self.world == 1:
@@ -90,25 +153,31 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, local_rank: int):
+    def __init__(self, local_rank: int, interval_ms: int = 50):
         cvd = os.environ.get("CUDA_VISIBLE_DEVICES", "")
         ids = [x for x in cvd.split(",") if x.strip()]
         self.index = ids[local_rank] if local_rank < len(ids) else str(local_rank)
+        self.interval_ms = interval_ms
         self.samples = []
         self.proc = None
         self.thread = None
 
-    def start(self):
+    def start(self, wait_first_s: float = 5.0):
+        """Start sampling and wait (bounded) for the first sample, so a short
+        timed region right after this call is covered."""
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", self.index],
+                 "-lms", str(self.interval_ms), "-i", self.index],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, ValueError):
             self.proc = None
             return
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
+        t0 = time.perf_counter()
+        while not self.samples and time.perf_counter() - t0 < wait_first_s:
+            time.sleep(0.02)
 
     def _read(self):
         for line in self.proc.stdout:
@@ -127,11 +196,13 @@ class ClockSampler:
             self.thread.join(timeout=5)
 
     def summary(self, t0: float, t1: float):
-        inside = [p for t, p in self.samples if t0 <= t <= t1 + 0.25]
+        pad = self.interval_ms / 1000.0
+        inside = [p for t, p in self.samples if t0 <= t <= t1 + pad]
         if not inside and self.samples:
             inside = [min(self.samples, key=lambda s: abs(s[0] - (t0 + t1) / 2))[1]]
         if not inside:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+
         def num(v):
             try:
                 return float(v)
@@ -143,7 +214,8 @@ class ClockSampler:
         pw = [num(p[3]) for p in inside if num(p[3]) is not None]
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": num(inside[0][2]), "reasons": reasons,
-                "power_w_max": max(pw) if pw else None, "samples": len(inside)}
+                "power_w_max": max(pw) if pw else None, "samples": len(inside),
+                "interval_ms": self.interval_ms}
 
 
 def load_peaks():
@@ -157,6 +229,70 @@ def load_peaks():
 
 
 # --------------------------------------------------------------------------
+# configurations (shared by both arms so their `config` keys are identical)
+# --------------------------------------------------------------------------
+GEMMS = {"bf16_gemm_8192": (8192, "bf16"), "bf16_gemm_4096": (4096, "bf16"),
+         "e4m3_gemm_8192": (8192, "e4m3")}
+SKINNY_N, SKINNY_K = 14336, 4096
+
+
+def gemm_copies(size: int, kind: str) -> int:
+    """Rotating copies of A and B so that consecutive steps never find their
+    operands in L2: one copy when A + B + C already exceed twice the L2."""
+    elem = 2 if kind == "bf16" else 1
+    ab = 2 * size * size * elem
+    if ab + size * size * 2 >= 2 * L2_BYTES:
+        return 1
+    return int(math.ceil(2 * L2_BYTES / ab))
+
+
+def skinny_copies(n_loc: int) -> int:
+    return max(3, int(math.ceil(3 * L2_BYTES / (SKINNY_K * n_loc * 2))))
+
+
+def config_for(name: str, world: int, gather: str = "fused") -> dict:
+    if name in GEMMS:
+        size, kind = GEMMS[name]
+        copies = gemm_copies(size, kind)
+        elem = 2 if kind == "bf16" else 1
+        ws = (2 * size * size * elem + size * size * 2) / (1 << 20)
+        return {
+            "workload": name, "M": size, "N": size, "K": size,
+            "dtype_in": kind, "dtype_out": "bf16", "accumulate": "fp32",
+            "parallelism": (f"A rows split over {world} GPUs, B replicated, C all-gathered "
+                            + ("inside the GEMM epilogue (P2P stores over NVLink + device flag "
+                               "barrier)" if gather == "fused" else "with NCCL")
+                            if world > 1 else "1 GPU"),
+            "l2_policy": (f"A + B + C = {ws:.0f} MiB > 2x L2 (126 MB): no flush needed"
+                          if copies == 1 else
+                          f"{copies} rotating copies of A and B "
+                          f"({copies * 2 * size * size * elem / (1 << 20):.0f} MiB) > 2x L2"),
+        }
+    if name.startswith("skinny_m"):
+        m = int(name[len("skinny_m"):])
+        n_loc0 = SKINNY_N if world == 1 else (lambda r: r[1] - r[0])(
+            _col_shard(SKINNY_N, world, 0))
+        return {
+            "workload": name, "M": m, "N": SKINNY_N, "K": SKINNY_K, "dtype_in": "bf16",
+            "dtype_out": "bf16", "accumulate": "fp32",
+            "parallelism": (f"W columns split over {world} GPUs, X replicated, Y not gathered"
+                            if world > 1 else "1 GPU"),
+            "l2_policy": f"{skinny_copies(n_loc0)} rotating copies of W (> 3x L2)",
+        }
+    if name == "add_f32":
+        return {"workload": name, "elements": 1 << 28, "dtype_in": "fp32",
+                "parallelism": f"contiguous ranges over {world} GPUs" if world > 1 else "1 GPU",
+                "l2_policy": "3 GiB of traffic per step (> L2)"}
+    raise SystemExit(f"unknown workload {name}")
+
+
+def _col_shard(n, world, rank, align=8):
+    base, extra = divmod(n // align, world)
+    s = rank * base + min(rank, extra)
+    return s * align, (s + base + (1 if rank < extra else 0)) * align
+
+
+# --------------------------------------------------------------------------
 # workloads
 # --------------------------------------------------------------------------
 def bf16_bits(x):
@@ -164,11 +300,29 @@ def bf16_bits(x):
     return dtypes.to_bf16_bits(x)
 
 
+def check_row_sample(m: int, world: int, dist_mod, total: int = CHECK_ROWS, seed: int = 1234):
+    """Sorted rows of C to check: the first and last row of every rank's
+    block plus seeded random rows inside it, ``total`` in all."""
+    rng = np.random.default_rng(seed)
+    per = max(2, total // world)
+    rows = []
+    for q in range(world):
+        s, e = dist_mod.row_shard(m, world, q)
+        pick = {s, e - 1}
+        if e - s > 2:
+            pick.update(int(x) for x in rng.choice(np.arange(s + 1, e - 1),
+                                                   size=min(per - 2, e - s - 2), replace=False))
+        rows.extend(sorted(pick))
+    return np.array(sorted(set(rows)), dtype=np.int64)
+
+
 class GemmWorkload:
     """bf16 / e4m3 GEMM, rows of A split over ranks, C all-gathered (fused
     into the GEMM epilogue over NVLink peer memory, or by NCCL)."""
 
-    def __init__(self, size: int, kind: str, d: Dist, rt, dist_mod, gather: str = "fused"):
+    def __init__(self, size: int, kind: str, d: Dist, rt, dist_mod, gather: str = "fused",
+                 comm=None):
+        self.name = f"{kind}_gemm_{size}"
         self.m = self.n = self.k = size
         self.kind = kind
         self.d = d
@@ -179,62 +333,116 @@ class GemmWorkload:
         rng = np.random.default_rng(0)
         a = rng.standard_normal((self.m, self.k), dtype=np.float32)
         b = rng.standard_normal((self.k, self.n), dtype=np.float32)
+        self.chk_rows = check_row_sample(self.m, d.world, dist_mod)
         if kind == "bf16":
             self.a_host = bf16_bits(a[self.start:self.stop])
             self.b_host = bf16_bits(b)
-            self.scale = 1.0
+            self.chk_a = bf16_bits(a[self.chk_rows])
+            self.sa = self.sb = 1.0
         else:
             from thork_b200 import dtypes
             # per-tensor scales of the full A and B (every rank draws the same
             # inputs), then this rank's rows
-            qa, sa = dtypes.quantize_e4m3(a)
+            qa, self.sa = dtypes.quantize_e4m3(a)
             self.a_host = np.ascontiguousarray(qa[self.start:self.stop])
-            self.b_host, sb = dtypes.quantize_e4m3(b)
-            self.scale = float(sa) * float(sb)
+            self.chk_a = np.ascontiguousarray(qa[self.chk_rows])
+            self.b_host, self.sb = dtypes.quantize_e4m3(b)
+            del qa
+        self.scale = float(self.sa) * float(self.sb)
         del a, b
         self.elem = self.a_host.dtype.itemsize
-        self.A = rt.DeviceArray.from_host(self.a_host)
-        self.B = rt.DeviceArray.from_host(self.b_host)
+        self.copies = gemm_copies(size, kind)
+        self.As = [rt.DeviceArray.from_host(self.a_host) for _ in range(self.copies)]
+        self.Bs = [rt.DeviceArray.from_host(self.b_host) for _ in range(self.copies)]
+        self.A, self.B = self.As[0], self.Bs[0]
+        self.i = 0
         self.gather = gather if d.world > 1 else "none"
         rows_out = self.m if d.world > 1 else self.m_loc
         self.C = rt.empty((rows_out, self.n), np.uint16) if self.gather != "fused" else None
-        self.comm = self.fg = None
+        self.comm = comm
+        self.own_comm = False
+        self.fg = None
         if d.world > 1:
-            uid = None
-            if d.rank == 0:
-                import ctypes
-                buf = (ctypes.c_uint8 * 128)()
-                rt.check(rt.lib().thork_nccl_get_unique_id(buf))
-                uid = bytes(buf)
-            uid = d.bcast_bytes(uid)
-            self.comm = dist_mod.Communicator(d.rank, d.world, unique_id=uid)
+            if self.comm is None:
+                uid = None
+                if d.rank == 0:
+                    import ctypes
+                    buf = (ctypes.c_uint8 * 128)()
+                    rt.check(rt.lib().thork_nccl_get_unique_id(buf))
+                    uid = bytes(buf)
+                uid = d.bcast_bytes(uid)
+                self.comm = dist_mod.Communicator(d.rank, d.world, unique_id=uid)
+                self.own_comm = True
             if self.gather == "fused":
                 self.fg = dist_mod.FusedGather(self.comm, self.m, self.n)
         # our kernels per step: the GEMM, plus the flag barrier when fused
         self.launches_per_step = 2 if self.gather == "fused" else 1
+        self.last = None
 
     flops_total = property(lambda self: 2.0 * self.m * self.n * self.k)
     flops_local = property(lambda self: 2.0 * self.m_loc * self.n * self.k)
+    # bytes of C one GPU sends to its peers per step (the all-gather)
+    gather_bytes_per_gpu = property(lambda self: 2.0 * self.m_loc * self.n * (self.d.world - 1))
+
+    def _operands(self):
+        a, b = self.As[self.i % self.copies], self.Bs[self.i % self.copies]
+        self.i += 1
+        return a, b
 
     def step(self, stream, ev0=None, ev1=None):
+        a, b = self._operands()
         if ev0 is not None:
             ev0.record(stream)
         if self.fg is not None:
-            self.fg.matmul(self.A, self.B, stream, gemm_done=ev1, dtype=self.kind,
-                           scale_a=self.scale)
+            self.last = self.fg.matmul(a, b, stream, gemm_done=ev1, dtype=self.kind,
+                                       scale_a=self.scale)
             return
-        self.dist.sharded_matmul(self.comm, self.A, self.B, self.C, self.m, dtype=self.kind,
+        self.dist.sharded_matmul(self.comm, a, b, self.C, self.m, dtype=self.kind,
                                  scale=self.scale, gather=self.d.world > 1, stream=stream,
                                  gemm_done=ev1)
+        self.last = self.C
 
     def local_step(self, stream, ev0=None, ev1=None):
         """This rank's GEMM alone, without the all-gather (scaling reference)."""
         if getattr(self, "C_loc", None) is None:
             self.C_loc = self.rt.empty((self.m_loc, self.n), np.uint16)
+        a, b = self._operands()
         if ev0 is not None:
             ev0.record(stream)
-        self.dist.sharded_matmul(None, self.A, self.B, self.C_loc, self.m_loc, dtype=self.kind,
+        self.dist.sharded_matmul(None, a, b, self.C_loc, self.m_loc, dtype=self.kind,
                                  scale=self.scale, gather=False, stream=stream, gemm_done=ev1)
+
+    def check(self, stream):
+        """One more step outside any timing; the sampled rows of the (gathered)
+        C against the oracle, and at N > 1 the whole gathered C bit for bit
+        against the NCCL all-gather path."""
+        from oracle import oracle
+        self.step(stream)
+        stream.synchronize()
+        c = self.last.to_host(stream=stream)
+        rows = self.chk_rows if self.d.world > 1 else self.chk_rows[self.chk_rows < self.m_loc]
+        got = oracle.bf16_bits_to_f32(c[rows - (0 if self.d.world > 1 else self.start)])
+        with all_host_threads():
+            if self.kind == "bf16":
+                ref = oracle.gemm_bf16_ref(self.chk_a, self.b_host)
+            else:
+                ref = oracle.gemm_e4m3_ref(self.chk_a, self.sa, self.b_host, self.sb)
+        if self.d.world == 1:
+            ref = ref[np.isin(self.chk_rows, rows)]
+        err = oracle.max_rel_err(got, ref)
+        out = {"max_rel_err": err, "rows": int(len(rows)), "tolerance": TOL,
+               "rows_from_every_rank": True,
+               "oracle": "fp32 NumPy matmul of the rounded (bf16) / dequantised (e4m3) inputs"}
+        if self.d.world > 1:
+            c_nccl = self.rt.empty((self.m, self.n), np.uint16)
+            self.dist.sharded_matmul(self.comm, self.A, self.B, c_nccl, self.m, dtype=self.kind,
+                                     scale=self.scale, gather=True, stream=stream)
+            stream.synchronize()
+            out["bitequal_vs_nccl"] = bool(np.array_equal(c_nccl.to_host(stream=stream), c))
+            del c_nccl
+        else:
+            out["bitequal_vs_nccl"] = None
+        return out
 
     def e2e_setup(self):
         rt = self.rt
@@ -263,7 +471,7 @@ class GemmWorkload:
 
     def cpu_sample(self, seconds: float):
         """The reference's check (NumPy fp32 matmul of the rounded inputs) on a
-        row sample of A; returns (TFLOP/s, sample description)."""
+        row sample of A; returns (TFLOP/s, sample description, rows)."""
         from oracle import oracle
         if self.kind == "bf16":
             a = oracle.bf16_bits_to_f32(self.a_host)
@@ -273,43 +481,55 @@ class GemmWorkload:
             b = oracle.e4m3_bits_to_f32(self.b_host) * np.float32(self.scale)
         return cpu_matmul_rate(a, b, seconds)
 
+    def close(self):
+        if self.fg is not None:
+            self.fg.close()
+            self.fg = None
+        if self.own_comm and self.comm is not None:
+            self.comm.close()
+            self.comm = None
 
-def cpu_matmul_rate(a, b, seconds):
-    rows = 64
-    t = 0.0
-    while True:  # calibrate a sample of about 1 s
+
+def cpu_matmul_rate(a, b, seconds, max_step_s=3.0):
+    """NumPy fp32 ``a @ b`` on every host core: the full ``a`` when one
+    product takes under ``max_step_s``, else a power-of-two row sample.
+    Returns (TFLOP/s, sample description, rows)."""
+    with all_host_threads():
+        rows = a.shape[0]
         t0 = time.perf_counter()
-        _ = a[:rows] @ b
+        _ = a[:min(rows, 256)] @ b
         t = time.perf_counter() - t0
-        if t > 0.5 or rows >= a.shape[0]:
-            break
-        rows = min(a.shape[0], rows * 4)
-    reps = max(1, int(seconds / max(t, 1e-6)))
-    t0 = time.perf_counter()
-    for _ in range(reps):
-        _ = a[:rows] @ b
-    dt_s = time.perf_counter() - t0
+        est = t * rows / min(rows, 256)
+        while est > max_step_s and rows > 64:
+            rows //= 2
+            est /= 2
+        reps = max(1, int(seconds / max(est, 1e-6)))
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            _ = a[:rows] @ b
+        dt_s = time.perf_counter() - t0
     flops = 2.0 * rows * a.shape[1] * b.shape[1] * reps
-    return flops / dt_s / 1e12, f"{reps} x ({rows}x{a.shape[1]} @ {a.shape[1]}x{b.shape[1]}) fp32 NumPy", rows
+    return (flops / dt_s / 1e12,
+            f"{reps} x ({rows}x{a.shape[1]} @ {a.shape[1]}x{b.shape[1]}) fp32 NumPy", rows)
 
 
 class SkinnyWorkload:
     """Decode GEMM Y = X.W (K=4096, N=14336); W split by columns over ranks,
-    three rotating copies of each W shard so no launch reads W from L2."""
+    rotating copies of each W shard so no launch reads W from L2."""
 
     def __init__(self, m: int, d: Dist, rt, dist_mod):
-        self.m, self.n, self.k = m, 14336, 4096
+        self.name = f"skinny_m{m}"
+        self.m, self.n, self.k = m, SKINNY_N, SKINNY_K
         self.d, self.rt = d, rt
         c0, c1 = dist_mod.col_shard(self.n, d.world, d.rank)
-        self.n_loc = c1 - c0
+        self.c0, self.n_loc = c0, c1 - c0
         rng = np.random.default_rng(0)
         w = rng.standard_normal((self.k, self.n), dtype=np.float32) * np.float32(0.02)
         x = rng.standard_normal((m, self.k), dtype=np.float32)
         self.x_host = bf16_bits(x)
         self.w_host = np.ascontiguousarray(bf16_bits(w[:, c0:c1]))
         self.X = rt.DeviceArray.from_host(self.x_host)
-        copies = max(3, int(np.ceil(3 * L2_BYTES / self.w_host.nbytes)))
-        self.W = [rt.DeviceArray.from_host(self.w_host) for _ in range(copies)]
+        self.W = [rt.DeviceArray.from_host(self.w_host) for _ in range(skinny_copies(self.n_loc))]
         self.Y = rt.empty((m, self.n_loc), np.uint16)
         self.i = 0
 
@@ -326,6 +546,18 @@ class SkinnyWorkload:
             self.X.ptr, w.ptr, self.Y.ptr, self.m, self.n_loc, self.k, 1, stream.handle))
         if ev1 is not None:
             ev1.record(stream)
+
+    def check(self, stream):
+        from oracle import oracle
+        self.Y.zero(stream)
+        self.step(stream)
+        stream.synchronize()
+        got = oracle.bf16_bits_to_f32(self.Y.to_host(stream=stream))
+        with all_host_threads():
+            ref = oracle.gemm_bf16_ref(self.x_host, self.w_host)
+        return {"max_rel_err": oracle.max_rel_err(got, ref), "rows": self.m,
+                "columns": f"{self.c0}..{self.c0 + self.n_loc} (this rank's block, all of them)",
+                "tolerance": TOL, "bitequal_vs_nccl": None}
 
     def e2e_setup(self):
         rt = self.rt
@@ -345,19 +577,25 @@ class SkinnyWorkload:
         from oracle import oracle
         x = oracle.bf16_bits_to_f32(self.x_host)
         w = oracle.bf16_bits_to_f32(self.w_host)
-        t0 = time.perf_counter()
-        reps = 0
-        while time.perf_counter() - t0 < seconds:
-            _ = x @ w
-            reps += 1
-        dt_s = time.perf_counter() - t0
-        return self.bytes_local * reps / dt_s / 1e9, f"{reps} x ({self.m}x{self.k} @ {self.k}x{self.n_loc}) fp32 NumPy", None
+        with all_host_threads():
+            t0 = time.perf_counter()
+            reps = 0
+            while time.perf_counter() - t0 < seconds:
+                _ = x @ w
+                reps += 1
+            dt_s = time.perf_counter() - t0
+        return (self.bytes_local * reps / dt_s / 1e9,
+                f"{reps} x ({self.m}x{self.k} @ {self.k}x{self.n_loc}) fp32 NumPy", None)
+
+    def close(self):
+        pass
 
 
 class AddWorkload:
     """out = A + B over 2^28 fp32 elements, split by contiguous ranges."""
 
     def __init__(self, n_total: int, d: Dist, rt, dist_mod):
+        self.name = "add_f32"
         self.n_total = n_total
         s, e = dist_mod.row_shard(n_total, d.world, d.rank)
         self.n = e - s
@@ -379,6 +617,16 @@ class AddWorkload:
                                                          self.n, stream.handle))
         if ev1 is not None:
             ev1.record(stream)
+
+    def check(self, stream):
+        from oracle import oracle
+        self.C.zero(stream)
+        self.step(stream)
+        stream.synchronize()
+        got = self.C.to_host(stream=stream)
+        exact = bool(np.array_equal(got, oracle.add_ref(self.a_host, self.b_host)))
+        return {"bitexact": exact, "elements": int(self.n), "max_rel_err": 0.0 if exact else 1.0,
+                "tolerance": 0.0, "bitequal_vs_nccl": None}
 
     def e2e_setup(self):
         rt = self.rt
@@ -404,14 +652,14 @@ class AddWorkload:
         dt_s = time.perf_counter() - t0
         return 12.0 * n * reps / dt_s / 1e9, f"{reps} x NumPy a+b over {n} fp32", None
 
+    def close(self):
+        pass
 
-def make_workload(name, d, rt, dist_mod, gather="fused"):
-    if name == "bf16_gemm_8192":
-        return GemmWorkload(8192, "bf16", d, rt, dist_mod, gather)
-    if name == "bf16_gemm_4096":
-        return GemmWorkload(4096, "bf16", d, rt, dist_mod, gather)
-    if name == "e4m3_gemm_8192":
-        return GemmWorkload(8192, "e4m3", d, rt, dist_mod, gather)
+
+def make_workload(name, d, rt, dist_mod, gather="fused", comm=None):
+    if name in GEMMS:
+        size, kind = GEMMS[name]
+        return GemmWorkload(size, kind, d, rt, dist_mod, gather, comm=comm)
     if name.startswith("skinny_m"):
         return SkinnyWorkload(int(name[len("skinny_m"):]), d, rt, dist_mod)
     if name == "add_f32":
@@ -419,27 +667,10 @@ def make_workload(name, d, rt, dist_mod, gather="fused"):
     raise SystemExit(f"unknown workload {name}")
 
 
-def describe(name, w, world):
+def unit_of(w):
     if isinstance(w, GemmWorkload):
-        return {
-            "workload": name, "M": w.m, "N": w.n, "K": w.k,
-            "dtype_in": w.kind, "dtype_out": "bf16", "accumulate": "fp32",
-            "parallelism": (f"A rows split over {world} GPUs, B replicated, C all-gathered "
-                            + ("inside the GEMM epilogue (P2P stores over NVLink + device flag "
-                               "barrier)" if w.gather == "fused" else "with NCCL")
-                            if world > 1 else "1 GPU"),
-            "l2_policy": "inputs+output larger than L2 (no flush needed)",
-        }, "TFLOP/s", "tensor"
-    if isinstance(w, SkinnyWorkload):
-        return {
-            "workload": name, "M": w.m, "N": w.n, "K": w.k, "dtype_in": "bf16",
-            "parallelism": (f"W columns split over {world} GPUs, X replicated, Y not gathered"
-                            if world > 1 else "1 GPU"),
-            "l2_policy": f"{len(w.W)} rotating copies of W (> 3x L2)",
-        }, "GB/s", "hbm"
-    return {"workload": name, "elements": w.n_total, "dtype_in": "fp32",
-            "parallelism": f"contiguous ranges over {world} GPUs" if world > 1 else "1 GPU",
-            "l2_policy": "3 GiB of traffic per step (> L2)"}, "GB/s", "hbm"
+        return "TFLOP/s", "tensor"
+    return "GB/s", "hbm"
 
 
 def time_steps(w, rt, steps, warmup, d, per_launch_events=True, sample_every=10):
@@ -474,19 +705,35 @@ def time_steps(w, rt, steps, warmup, d, per_launch_events=True, sample_every=10)
     return total_ms, kernel_ms, t_wall0, t_wall1
 
 
+def checked(d, chk):
+    """Combine one check over ranks: worst error, and bit-equality on all."""
+    chk = dict(chk)
+    chk["max_rel_err"] = d.max(float(chk.get("max_rel_err", 0.0)))
+    if chk.get("bitequal_vs_nccl") is not None:
+        chk["bitequal_vs_nccl"] = d.min(1.0 if chk["bitequal_vs_nccl"] else 0.0) == 1.0
+    if "bitexact" in chk:
+        chk["bitexact"] = d.min(1.0 if chk["bitexact"] else 0.0) == 1.0
+    chk["max_rel_err"] = float(f"{chk['max_rel_err']:.3e}")
+    chk["ranks"] = d.world
+    chk["pass"] = (chk["max_rel_err"] <= chk.get("tolerance", TOL)
+                   and chk.get("bitequal_vs_nccl") is not False
+                   and chk.get("bitexact", True) is not False)
+    return chk
+
+
 def run_thork(args, d: Dist):
     import thork_b200 as tk
     from thork_b200 import dist as dist_mod
     rt = tk.runtime
     rt.set_device(d.local_rank)
     peaks, peak_src = load_peaks()
-    w = make_workload(args.workload, d, rt, dist_mod, args.gather)
-    cfg, unit, bound = describe(args.workload, w, d.world)
-
     sampler = ClockSampler(d.local_rank)
     sampler.start()
+    w = make_workload(args.workload, d, rt, dist_mod, args.gather)
+    cfg = config_for(args.workload, d.world, args.gather)
+    unit, bound = unit_of(w)
+
     total_ms, kernel_ms, tw0, tw1 = time_steps(w, rt, args.steps, args.warmup, d)
-    sampler.stop()
     clocks = sampler.summary(tw0, tw1)
     ms_step = d.max(total_ms / args.steps)
 
@@ -533,7 +780,7 @@ def run_thork(args, d: Dist):
         "data": "synthetic: seeded N(0,1) inputs (target shapes and distributions), host-rounded",
         "config": cfg,
         "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": round(peak, 1),
-                     "unit": unit.replace("TFLOP/s", "TFLOP/s"), "frac": round(achieved / peak, 4),
+                     "unit": unit, "frac": round(achieved / peak, 4),
                      "traffic": None, "peak_source": peak_note, "algorithmic": alg,
                      "kernel_ms": round(kernel_ms, 5)},
         "e2e": {"value": round(e2e_val, 3), "unit": unit, "h2d_bytes_per_step": int(w.h2d),
@@ -548,63 +795,110 @@ def run_thork(args, d: Dist):
         loc_ms, _, _, _ = time_steps(types.SimpleNamespace(step=w.local_step), rt, args.steps,
                                      args.warmup, d, per_launch_events=False)
         loc_step = d.max(loc_ms / args.steps)
-        line["without_gather"] = {"value": round(w.flops_total / (loc_step * 1e-3) / 1e12, 2),
-                                  "unit": unit, "ms_per_step": round(loc_step, 5),
-                                  "gather_ms_per_step": round(ms_step - loc_step, 5)}
+        gb = w.gather_bytes_per_gpu
+        line["without_gather"] = {
+            "value": round(w.flops_total / (loc_step * 1e-3) / 1e12, 2), "unit": unit,
+            "ms_per_step": round(loc_step, 5),
+            "gather_ms_per_step": round(ms_step - loc_step, 5),
+            "gather_bytes_per_gpu": int(gb),
+            # what each GPU pushes over NVLink per step, over the whole step and
+            # over the part of the step the gather adds to the GEMM
+            "gather_GBps_per_gpu": round(gb / (ms_step * 1e-3) / 1e9, 1),
+            "gather_GBps_per_gpu_exposed": (round(gb / ((ms_step - loc_step) * 1e-3) / 1e9, 1)
+                                            if ms_step > loc_step else None),
+        }
+    line["check"] = checked(d, w.check(rt.Stream()))
     if d.rank == 0 and d.world == 1:
         v, sample, _ = w.cpu_sample(args.cpu_seconds)
+        nthreads, blas = blas_threads()
         line["cpu_baseline"] = {"value": round(v, 4), "unit": unit, "cores": os.cpu_count(),
                                 "kind": "port", "sample": sample,
-                                "threads": os.environ.get("OPENBLAS_NUM_THREADS", "all")}
-        if args.also:
-            line["also"] = also_measurements(args, d, rt, dist_mod, peaks)
+                                "threads": os.cpu_count() if unit == "TFLOP/s" else 1,
+                                "blas": blas}
+    if args.also:
+        line["also"] = also_measurements(args, d, rt, dist_mod, peaks, main=w, sampler=sampler,
+                                         ms_step=ms_step)
+    sampler.stop()
     traffic = traffic_from_profiles(args.workload) if d.world == 1 else None
     if traffic is not None:
         line["roofline"]["traffic"] = traffic
-    if w.__class__ is GemmWorkload and w.comm is not None:
-        if w.fg is not None:
-            w.fg.close()
-        w.comm.close()
+    w.close()
+    failed = [k for k, v in [("main", line["check"])] + [
+        (k, v.get("check")) for k, v in line.get("also", {}).items() if isinstance(v, dict)]
+        if v is not None and not v.get("pass", True)]
+    if failed:
+        line["check_failed"] = failed
     if d.rank == 0:
         print(json.dumps(line), flush=True)
+    return 1 if failed else 0
 
 
-def also_measurements(args, d, rt, dist_mod, peaks):
-    """Short device-resident timings of the other target configurations (1 GPU)."""
+def _also_entry(w, d, rt, peaks, steps):
+    total_ms, kernel_ms, _, _ = time_steps(w, rt, steps, 10, d, per_launch_events=False)
+    ms = d.max(kernel_ms)
+    if isinstance(w, GemmWorkload):
+        v = w.flops_total / (ms * 1e-3) / 1e12
+        peak = peaks["bf16_tflops"] * (2.0 if w.kind == "e4m3" else 1.0) * d.world
+        out = {"TFLOP/s": round(v, 1), "frac_of_peak": round(v / peak, 3), "ms": round(ms, 4),
+               "peak": (f"{d.world} x " if d.world > 1 else "")
+               + ("2 x measured bf16 burst (no measured FP8 peak)" if w.kind == "e4m3"
+                  else "measured bf16 burst"),
+               "l2_policy": config_for(w.name, d.world)["l2_policy"]}
+    else:
+        v = w.bytes_total / (ms * 1e-3) / 1e9
+        per_gpu = w.bytes_local / (kernel_ms * 1e-3) / 1e9
+        out = {"GB/s": round(v, 1), "us": round(ms * 1e3, 2),
+               "GB/s_per_gpu": round(per_gpu, 1),
+               "frac_of_hbm": round(d.min(per_gpu) / peaks["hbm_gbs"], 3)}
+    out["check"] = checked(d, w.check(rt.Stream()))
+    return out
+
+
+def also_measurements(args, d, rt, dist_mod, peaks, main=None, sampler=None, ms_step=None):
+    """Short device-resident timings of the other target configurations.  At
+    N = 1: every config, a sustained run of the headline GEMM, config 0 and
+    the traced tile matmul.  At N > 1: the multi-GPU configs (FP8 8192^3 with
+    the fused all-gather, decode GEMMs with W split by columns)."""
     out = {}
-    for name, steps in (("e4m3_gemm_8192", 100), ("bf16_gemm_4096", 200), ("skinny_m1", 300),
-                        ("skinny_m16", 300), ("skinny_m128", 300), ("add_f32", 100)):
-        w = make_workload(name, d, rt, dist_mod)
-        total_ms, kernel_ms, _, _ = time_steps(w, rt, steps, 10, d, per_launch_events=False)
-        if isinstance(w, GemmWorkload):
-            v = w.flops_total / (kernel_ms * 1e-3) / 1e12
-            peak = peaks["bf16_tflops"] * (2.0 if w.kind == "e4m3" else 1.0)
-            out[name] = {"TFLOP/s": round(v, 1), "frac_of_peak": round(v / peak, 3),
-                         "ms": round(kernel_ms, 4)}
-        else:
-            v = w.bytes_total / (kernel_ms * 1e-3) / 1e9
-            out[name] = {"GB/s": round(v, 1), "frac_of_hbm": round(v / peaks["hbm_gbs"], 3),
-                         "us": round(kernel_ms * 1e3, 2)}
+    if d.world == 1:
+        plan = (("e4m3_gemm_8192", 100), ("bf16_gemm_4096", 200), ("skinny_m1", 300),
+                ("skinny_m16", 300), ("skinny_m128", 300), ("add_f32", 100))
+    else:
+        plan = (("e4m3_gemm_8192", 100), ("skinny_m1", 300), ("skinny_m16", 300),
+                ("skinny_m128", 300))
+    comm = main.comm if isinstance(main, GemmWorkload) else None
+    for name, steps in plan:
+        w = make_workload(name, d, rt, dist_mod, comm=comm)
+        out[name] = _also_entry(w, d, rt, peaks, steps)
+        w.close()
         del w
-    # config 0: 1024 x 1024 fp32 add (12.6 MB, L2-resident; latency-bound)
-    a = rt.to_device(np.ones((1 << 20,), np.float32))
-    c = rt.empty((1 << 20,), np.float32)
+    if d.world > 1:
+        return out
+    if isinstance(main, GemmWorkload) and ms_step:
+        out[main.name + "_sustained"] = sustained_run(main, rt, d, peaks, sampler, ms_step)
+    # config 0: 1024 x 1024 fp32 add of the config's seeded N(0,1) arrays
+    # (12.6 MB, L2-resident; latency-bound)
+    from oracle import oracle
+    ah, bh = oracle.add_inputs((1024, 1024), seed=0)
+    a, b = rt.to_device(ah), rt.to_device(bh)
+    c = rt.empty((1024, 1024), np.float32)
     s = rt.Stream()
     e0, e1 = rt.Event(), rt.Event()
     for _ in range(10):
-        rt.lib().thork_matrix_add_f32(c.ptr, a.ptr, a.ptr, 1 << 20, s.handle)
+        rt.lib().thork_matrix_add_f32(c.ptr, a.ptr, b.ptr, 1 << 20, s.handle)
     e0.record(s)
     for _ in range(200):
-        rt.lib().thork_matrix_add_f32(c.ptr, a.ptr, a.ptr, 1 << 20, s.handle)
+        rt.lib().thork_matrix_add_f32(c.ptr, a.ptr, b.ptr, 1 << 20, s.handle)
     e1.record(s)
     e1.synchronize()
     us = e0.elapsed_ms(e1) / 200 * 1e3
+    exact = bool(np.array_equal(c.to_host(stream=s), oracle.add_ref(ah, bh)))
     out["add_f32_1024x1024"] = {"GB/s": round(12 * (1 << 20) / us / 1e3, 1), "us": round(us, 2),
-                                "note": "L2-resident, launch-latency bound"}
+                                "note": "L2-resident, launch-latency bound",
+                                "check": {"bitexact": exact, "max_rel_err": 0.0 if exact else 1.0,
+                                          "tolerance": 0.0, "pass": exact}}
     # the same config through the drop-in call with NumPy arrays (copy-in, launch, copy-back)
     import thork_b200 as tk
-    ah = np.random.default_rng(0).standard_normal((1024, 1024), dtype=np.float32)
-    bh = np.random.default_rng(1).standard_normal((1024, 1024), dtype=np.float32)
     ch = np.empty_like(ah)
     add = tk.kernels.matrix_add((1024, 1024))
     for _ in range(5):
@@ -619,12 +913,24 @@ def also_measurements(args, d, rt, dist_mod, peaks):
     return out
 
 
+def sustained_run(w, rt, d, peaks, sampler, ms_step, seconds=2.5):
+    """The headline GEMM back to back for ``seconds`` (CUDA events around the
+    run, clocks sampled inside it): the number under the 1 kW power cap."""
+    steps = max(100, int(seconds * 1e3 / max(ms_step, 1e-3)))
+    total_ms, _, t0, t1 = time_steps(w, rt, steps, 10, d, per_launch_events=False)
+    clocks = sampler.summary(t0, t1) if sampler is not None else None
+    v = w.flops_total / (total_ms / steps * 1e-3) / 1e12
+    return {"TFLOP/s": round(v, 1), "steps": steps, "seconds": round(total_ms / 1e3, 3),
+            "frac_of_sustained_peak": round(v / peaks["bf16_tflops_sustained"], 3),
+            "peak": "measured bf16 sustained (cuBLAS, seconds-long loop)", "clocks": clocks}
+
+
 def traced_tile_gemm(tk, rt, peaks, size=4096):
     """A user-written @tk.jit tile matmul in the style of the reference's
     level-06 tcgen05 test kernel (one 128x128 output tile per CTA, a
     single-stage TMA -> tcgen05.mma loop, TMEM -> registers -> shared -> TMA
-    store), timed device-resident: the traced tile path, not the library
-    GEMM."""
+    store), timed device-resident with CUDA events on the launch stream: the
+    traced tile path, not the library GEMM."""
     G = tk.kittens.Global
     bf = tk.dt.bfloat16
     TM, TN, TK = 128, 128, 64
@@ -685,15 +991,42 @@ def traced_tile_gemm(tk, rt, peaks, size=4096):
     D = rt.empty((m, n), np.uint16)
     launch = tile_mm[((m // TM) * (n // TN), 1, 1), (128, 1, 1)]
     launch(A, B, D, k, n)  # trace + NVRTC compile
-    reps = 20
-    t0 = time.perf_counter()
+    out = time_traced(launch, (A, B, D, k, n), rt, 2.0 * m * n * k, peaks,
+                      "reference level-06 style: single stage, 128x128 tile per CTA")
+    out["check"] = check_gemm_rows(D, A, B, rt)
+    return out
+
+
+def check_gemm_rows(D, A, B, rt, nrows=CHECK_ROWS):
+    """Seeded rows of a bf16 C = A.B on the device against the oracle."""
+    from oracle import oracle
+    m = D.shape[0]
+    rows = np.sort(np.random.default_rng(99).choice(m, size=min(nrows, m), replace=False))
+    a = A.to_host()[rows]
+    with all_host_threads():
+        ref = oracle.gemm_bf16_ref(a, B.to_host())
+    err = oracle.max_rel_err(oracle.bf16_bits_to_f32(D.to_host()[rows]), ref)
+    return {"max_rel_err": float(f"{err:.3e}"), "rows": int(len(rows)), "tolerance": TOL,
+            "pass": err <= TOL}
+
+
+def time_traced(launch, args, rt, flops, peaks, note, reps=20):
+    """Device time of a traced launch: CUDA events on the stream the drop-in
+    call launches on, around each (synchronous) call."""
+    s = rt._dispatch_stream()
+    times = []
     for _ in range(reps):
-        launch(A, B, D, k, n)
-    ms = (time.perf_counter() - t0) / reps * 1e3  # launches are synchronous
-    tf = 2.0 * m * n * k / (ms * 1e-3) / 1e12
+        e0, e1 = rt.Event(), rt.Event()
+        e0.record(s)
+        launch(*args)
+        e1.record(s)
+        e1.synchronize()
+        times.append(e0.elapsed_ms(e1))
+    ms = statistics.median(times)
+    tf = flops / (ms * 1e-3) / 1e12
     return {"TFLOP/s": round(tf, 1), "ms": round(ms, 4),
-            "frac_of_peak": round(tf / peaks["bf16_tflops"], 3),
-            "note": "user-style traced kernel; each launch synchronises like the reference's"}
+            "frac_of_peak": round(tf / peaks["bf16_tflops"], 3), "note": note,
+            "timing": "median of CUDA-event device times around each drop-in launch"}
 
 
 def traffic_from_profiles(workload):
@@ -707,24 +1040,26 @@ def traffic_from_profiles(workload):
 
 
 def run_reference(args, d: Dist):
-    """The reference's CPU path (NumPy verification arithmetic), rank 0 only."""
+    """The reference's CPU path (NumPy verification arithmetic), rank 0 only,
+    every host core; the same problem at every N (the CPU does the whole job)."""
     if d.rank != 0:
-        return
+        return 0
     from oracle import oracle
     name = args.workload
     steps = args.steps + args.warmup
-    per_step = max(0.05, min(2.0, 90.0 / max(steps, 1)))
-    if name in ("bf16_gemm_8192", "bf16_gemm_4096", "e4m3_gemm_8192"):
-        size = 8192 if name.endswith("8192") else 4096
+    nthreads, blas = blas_threads()
+    if name in GEMMS:
+        size, kind = GEMMS[name]
         a, b = oracle.gemm_inputs(size, size, size, seed=0)
-        if name.startswith("e4m3"):
+        if kind == "e4m3":
             qa, sa = oracle.quantize_e4m3(a)
             qb, sb = oracle.quantize_e4m3(b)
             a = oracle.e4m3_bits_to_f32(qa) * sa
             b = oracle.e4m3_bits_to_f32(qb) * sb
         else:
             a, b = oracle.round_bf16(a), oracle.round_bf16(b)
-        rate, _, rows = cpu_matmul_rate(a, b, per_step)
+        # the whole product per step unless one takes over ~90 s / steps
+        _, _, rows = cpu_matmul_rate(a, b, 0.0, max_step_s=max(0.05, min(3.0, 90.0 / steps)))
         times = []
         for i in range(steps):
             t0 = time.perf_counter()
@@ -732,10 +1067,11 @@ def run_reference(args, d: Dist):
             times.append(time.perf_counter() - t0)
         t = statistics.median(times[args.warmup:] or times)
         value, unit = 2.0 * rows * size * size / t / 1e12, "TFLOP/s"
-        sample = f"rows 0..{rows} of A ({rows}x{size} @ {size}x{size}) fp32 NumPy per step"
+        sample = (f"rows 0..{rows} of A ({rows}x{size} @ {size}x{size}) fp32 NumPy per step"
+                  + (" (the whole product)" if rows == size else ""))
     elif name.startswith("skinny_m"):
         m = int(name[len("skinny_m"):])
-        x, w = oracle.skinny_inputs(m, 14336, 4096, seed=0)
+        x, w = oracle.skinny_inputs(m, SKINNY_N, SKINNY_K, seed=0)
         x, w = oracle.round_bf16(x), oracle.round_bf16(w)
         times = []
         for _ in range(steps):
@@ -743,8 +1079,8 @@ def run_reference(args, d: Dist):
             _ = x @ w
             times.append(time.perf_counter() - t0)
         t = statistics.median(times[args.warmup:] or times)
-        value, unit = 2.0 * (4096 * 14336 + m * 4096 + m * 14336) / t / 1e9, "GB/s"
-        sample = f"full ({m}x4096 @ 4096x14336) fp32 NumPy per step"
+        value, unit = 2.0 * (SKINNY_K * SKINNY_N + m * SKINNY_K + m * SKINNY_N) / t / 1e9, "GB/s"
+        sample = f"full ({m}x{SKINNY_K} @ {SKINNY_K}x{SKINNY_N}) fp32 NumPy per step"
     else:
         n = 1 << 26
         a, b = oracle.add_inputs((n,), seed=0)
@@ -756,29 +1092,25 @@ def run_reference(args, d: Dist):
         t = statistics.median(times[args.warmup:] or times)
         value, unit = 12.0 * n / t / 1e9, "GB/s"
         sample = f"NumPy a+b over {n} fp32 (2^26 of the 2^28 elements) per step"
-    cfg = {"workload": name, "parallelism": "host CPU (rank 0)",
-           "threads": os.environ.get("OPENBLAS_NUM_THREADS", "all cores")}
-    # the same problem keys as this benchmark's own arm
-    if name in ("bf16_gemm_8192", "bf16_gemm_4096", "e4m3_gemm_8192"):
-        cfg.update({"M": size, "N": size, "K": size, "dtype_in": name.split("_")[0],
-                    "compute": "fp32 NumPy matmul of the rounded inputs"})
-    elif name.startswith("skinny_m"):
-        cfg.update({"M": m, "N": 14336, "K": 4096, "dtype_in": "bf16",
-                    "compute": "fp32 NumPy matmul of the rounded inputs"})
-    else:
-        cfg.update({"elements": 1 << 28, "dtype_in": "fp32", "compute": "NumPy a + b"})
+        nthreads = 1
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": unit,
         "n_gpus": d.world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(t * 1e3, 4), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic: seeded N(0,1), host-rounded",
-        "config": cfg,
+        "vs_baseline": None,
+        "dtype": {"bf16_gemm_8192": "bf16", "bf16_gemm_4096": "bf16", "e4m3_gemm_8192": "e4m3"}.get(
+            name, "bf16" if name.startswith("skinny") else "f32"),
+        "data": "synthetic: seeded N(0,1) inputs (target shapes and distributions), host-rounded",
+        # the same config as the thork arm at this N (the CPU computes the whole job)
+        "config": config_for(name, d.world, args.gather),
         "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": os.cpu_count(),
-                         "kind": "port", "sample": sample},
+                         "threads": nthreads, "blas": blas, "kind": "port", "sample": sample,
+                         "compute": "fp32 NumPy on the host (the reference's verification path)"},
         "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+    return 0
 
 
 def main():
@@ -799,13 +1131,17 @@ def main():
     d = Dist()
     if d.world != args.gpus:
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE={d.world}", file=sys.stderr)
+    rc = 0
     try:
         if args.impl == "reference":
-            run_reference(args, d)
+            rc = run_reference(args, d)
         else:
-            run_thork(args, d)
+            rc = run_thork(args, d)
     finally:
         d.close()
+    if rc:
+        print("bench: a result check failed (see check_failed in the JSON line)", file=sys.stderr)
+    sys.exit(rc)
 
 
 if __name__ == "__main__":

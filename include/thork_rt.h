@@ -113,6 +113,10 @@ THORK_API int thork_memcpy_htod(void *d_dst, const void *h_src, size_t nbytes, v
 THORK_API int thork_memcpy_dtoh(void *h_dst, const void *d_src, size_t nbytes, void *stream, int sync);
 THORK_API int thork_memcpy_dtod(void *d_dst, const void *d_src, size_t nbytes, void *stream);
 THORK_API int thork_memset(void *d_ptr, int value, size_t nbytes, void *stream);
+/* Free and total device memory of the current device (cudaMemGetInfo).  No
+ * reference counterpart; tests use it to show an entry point allocates
+ * nothing.                                                                 */
+THORK_API int thork_mem_info(size_t *free_bytes, size_t *total_bytes);
 
 /* ---- streams and events (no reference counterpart: it uses stream 0) --- */
 THORK_API int thork_stream_create(void **stream);
@@ -288,9 +292,21 @@ THORK_API int thork_skinny_gemm_bf16_ex(const void *d_x, const void *d_w, void *
  *     partials, two slots per CTA, always fit); larger requests return
  *     THORK_ERR_INVALID with the sizes in the message.  Inputs, output and
  *     stream are as for thork_skinny_gemm_bf16; no cudaMalloc, cudaFree or
- *     other allocating call is made.                                       */
+ *     other allocating call is made.
+ *   - Failures: a bounded wait that expires inside this kernel is recorded
+ *     in a status word inside the same scratch array, NOT in the word that
+ *     thork_kernel_status reads.  Read it with
+ *     thork_skinny_gemm_bf16_noalloc_status; it is sticky (later calls do
+ *     not clear it), so a non-zero value means some call since the last
+ *     clearing read may have left Y incomplete.                            */
 THORK_API int thork_skinny_gemm_bf16_noalloc(const void *d_x, const void *d_w, void *d_y,
                                             int M, int N, int K, void *stream);
+/* Status word of thork_skinny_gemm_bf16_noalloc on the current device: waits
+ * for `stream`, copies the word into *status (0 = every call since the last
+ * clear finished its waits; else code in bits 0-7, wait site in bits 8-15)
+ * and resets it when clear != 0.  Allocates nothing.  No reference
+ * counterpart.                                                             */
+THORK_API int thork_skinny_gemm_bf16_noalloc_status(unsigned *status, int clear, void *stream);
 
 /* ---- NCCL (dlopen of libnccl.so.2; no reference counterpart) ---------- */
 /* Writes a 128-byte ncclUniqueId into id128.                              */

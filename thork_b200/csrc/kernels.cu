@@ -673,8 +673,10 @@ extern "C" int thork_skinny_gemm_bf16(const void *d_x, const void *d_w, void *d_
 // allocation-free decode GEMM (thork_skinny_gemm_bf16_noalloc)
 // ---------------------------------------------------------------------------
 // Scratch layout: [status word, 256 B][tile counters, 64 KiB][partial slots].
-// The array is zero when the library's module loads; each call clears the
-// status word and the counters it will use before launching.
+// The array is zero when the library's module loads.  Each call clears the
+// counters it will use before launching; the status word is sticky: kernels
+// only OR a code into it, and only thork_skinny_gemm_bf16_noalloc_status
+// (clear != 0) resets it, so an expired wait stays visible until read.
 namespace {
 constexpr size_t kNoAllocBytes = 8u << 20;
 constexpr size_t kNoAllocStatusBytes = 256;
@@ -719,8 +721,9 @@ int run_skinny_noalloc(int kernel_id, const void *d_x, const void *d_w, void *d_
   if ((rc = noalloc_scratch(&base))) return rc;
   unsigned char *counters = base + kNoAllocStatusBytes;
   unsigned char *partial = counters + kNoAllocCounterBytes;
-  // the status word and this plan's tile counters must start at zero
-  cudaError_t e = cudaMemsetAsync(base, 0, kNoAllocStatusBytes + pl.counter_bytes, s);
+  // this plan's tile counters must start at zero (the status word is left
+  // as it is: it keeps any earlier call's expired-wait code until read)
+  cudaError_t e = cudaMemsetAsync(counters, 0, pl.counter_bytes, s);
   if (e != cudaSuccess) return thork_cuda_error(e, "cudaMemsetAsync(no-alloc scratch)");
   alignas(64) TensorMap ta, tb;
   if ((rc = encode_skinny_maps<Cfg>(ta, tb, d_x, d_w, M, N, K))) return rc;
@@ -747,4 +750,25 @@ extern "C" int thork_skinny_gemm_bf16_noalloc(const void *d_x, const void *d_w, 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (M <= 16) return run_skinny_noalloc<CfgSkinny16>(K_SKSK16, d_x, d_w, d_y, M, N, K, s);
   return run_skinny_noalloc<CfgSkinny32>(K_SKSK32, d_x, d_w, d_y, M, N, K, s);
+}
+
+extern "C" int thork_skinny_gemm_bf16_noalloc_status(unsigned *status, int clear, void *stream) {
+  if (!status) return thork_set_error(THORK_ERR_INVALID, "noalloc_status: status is NULL");
+  unsigned char *base;
+  int rc;
+  if ((rc = noalloc_scratch(&base))) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // a 4-byte copy into the caller's host word and an optional 4-byte clear:
+  // neither allocates device or pinned memory
+  cudaError_t e = cudaMemcpyAsync(status, base, sizeof(unsigned), cudaMemcpyDeviceToHost, s);
+  if (e != cudaSuccess) return thork_cuda_error(e, "read no-alloc status word");
+  e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return thork_cuda_error(e, "cudaStreamSynchronize(no-alloc status)");
+  if (clear) {
+    e = cudaMemsetAsync(base, 0, sizeof(unsigned), s);
+    if (e != cudaSuccess) return thork_cuda_error(e, "clear no-alloc status word");
+    e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return thork_cuda_error(e, "cudaStreamSynchronize(no-alloc status)");
+  }
+  return THORK_OK;
 }

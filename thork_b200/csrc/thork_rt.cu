@@ -237,6 +237,11 @@ extern "C" int thork_memcpy_dtoh(void *h_dst, const void *d_src, size_t n, void 
 extern "C" int thork_memcpy_dtod(void *d_dst, const void *d_src, size_t n, void *stream) {
   return do_copy(d_dst, d_src, n, cudaMemcpyDeviceToDevice, stream, 0, "memcpy DtoD");
 }
+extern "C" int thork_mem_info(size_t *free_bytes, size_t *total_bytes) {
+  if (!free_bytes || !total_bytes) return thork_set_error(THORK_ERR_INVALID, "mem_info: NULL output");
+  CUDA_TRY(cudaMemGetInfo(free_bytes, total_bytes), "cudaMemGetInfo");
+  return THORK_OK;
+}
 extern "C" int thork_memset(void *d_ptr, int value, size_t n, void *stream) {
   if (n == 0) return THORK_OK;
   CUDA_TRY(cudaMemsetAsync(d_ptr, value, n, static_cast<cudaStream_t>(stream)), "cudaMemsetAsync");

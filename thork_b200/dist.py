@@ -284,12 +284,12 @@ class FusedGather:
 
 def _gemm_launcher(dtype: str, m: int, n: int, k: int, scale: float = 1.0) -> Callable:
     L = rt.lib()
+    # whole 128 x 256 tiles (variant 1), as in the fused all-gather, so both
+    # ways of gathering C produce the same bits
     if dtype == "bf16":
-        # whole 128 x 256 tiles (variant 1), as in the fused all-gather, so both
-        # ways of gathering C produce the same bits
         return lambda a, b, c, s: L.thork_gemm_bf16(a, b, c, m, n, k, 1, s)
     if dtype == "e4m3":
-        return lambda a, b, c, s: L.thork_gemm_e4m3(a, b, c, m, n, k, float(scale), 1.0, 0, s)
+        return lambda a, b, c, s: L.thork_gemm_e4m3(a, b, c, m, n, k, float(scale), 1.0, 1, s)
     raise ValueError(f"unknown GEMM dtype {dtype!r}")
 
 

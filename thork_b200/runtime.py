@@ -64,6 +64,7 @@ _SIGNATURES = {
     "thork_memcpy_dtoh": [_vp, _vp, _sz, _vp, _i],
     "thork_memcpy_dtod": [_vp, _vp, _sz, _vp],
     "thork_memset": [_vp, _i, _sz, _vp],
+    "thork_mem_info": [ctypes.POINTER(_sz), ctypes.POINTER(_sz)],
     "thork_stream_create": [_pvp],
     "thork_stream_destroy": [_vp],
     "thork_stream_synchronize": [_vp],
@@ -91,6 +92,7 @@ _SIGNATURES = {
     "thork_gemm_e4m3": [_vp, _vp, _vp, _i, _i, _i, ctypes.c_float, ctypes.c_float, _i, _vp],
     "thork_skinny_gemm_bf16": [_vp, _vp, _vp, _i, _i, _i, _vp],
     "thork_skinny_gemm_bf16_noalloc": [_vp, _vp, _vp, _i, _i, _i, _vp],
+    "thork_skinny_gemm_bf16_noalloc_status": [ctypes.POINTER(_u), _i, _vp],
     "thork_skinny_gemm_bf16_ex": [_vp, _vp, _vp, _i, _i, _i, _i, _vp],
     "thork_gemm_bf16_allgather": [_vp, _vp, _vp, _pvp, _i, _i, _i, _i, _i, _vp, ctypes.c_uint, _i,
                                   _vp],
@@ -448,6 +450,26 @@ def status_pointer() -> int:
     p = ctypes.c_void_p()
     check(lib().thork_status_pointer(ctypes.byref(p)), "status pointer")
     return p.value
+
+
+def mem_info() -> Tuple[int, int]:
+    """(free, total) bytes of device memory on the current device."""
+    get_device()
+    f, t = ctypes.c_size_t(0), ctypes.c_size_t(0)
+    check(lib().thork_mem_info(ctypes.byref(f), ctypes.byref(t)), "mem info")
+    return f.value, t.value
+
+
+def noalloc_status(clear: bool = True, stream: Optional["Stream"] = None) -> int:
+    """Status word of the allocation-free decode GEMM
+    (``thork_skinny_gemm_bf16_noalloc``), which keeps its own word inside its
+    static scratch array: non-zero after a bounded wait in one of its calls
+    expired.  The word is sticky until read with ``clear``."""
+    get_device()
+    v = ctypes.c_uint(0)
+    check(lib().thork_skinny_gemm_bf16_noalloc_status(
+        ctypes.byref(v), 1 if clear else 0, stream.handle if stream else None), "no-alloc status")
+    return v.value
 
 
 # --------------------------------------------------------------------------
