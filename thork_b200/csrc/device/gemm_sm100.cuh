@@ -917,17 +917,6 @@ struct Config2 {
   static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
 };
 
-// 2-D tiled load whose completion is counted on a barrier of the leader CTA
-// (cta_group::2 form; `bar_cluster` is a shared::cluster address).
-__device__ __forceinline__ void tma_load_2d_pair(u32 dst, const TensorMap *m, u32 bar_cluster, int x,
-                                                 int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
-      "l"(reinterpret_cast<u64>(m)), "r"(bar_cluster), "r"(x), "r"(y)
-      : "memory");
-}
-
 template <class Cfg>
 __global__ void __launch_bounds__(192, 1)
     gemm2_kernel(const __grid_constant__ TensorMap tmap_a, const __grid_constant__ TensorMap tmap_b,

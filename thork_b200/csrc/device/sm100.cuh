@@ -143,6 +143,18 @@ __device__ __forceinline__ void tma_load_2d(u32 dst, const TensorMap *m, u32 bar
 }
 
 // 2-D tiled store of a shared-memory box to global memory (bulk group).
+// 2-D tiled load into this CTA's shared memory whose completion is counted
+// on a barrier of either CTA of a cluster pair (cta_group::2 form;
+// `bar_cluster` is a shared::cluster address).  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(u32 dst, const TensorMap *m, u32 bar_cluster, int x,
+                                                 int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<u64>(m)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_store_2d(const TensorMap *m, u32 src, int x, int y) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::
                    "l"(reinterpret_cast<u64>(m)),

@@ -475,6 +475,37 @@ __device__ __forceinline__ void tmem_release(u32 *slot) {
   if (threadIdx.x / 32 == 0) tmem_dealloc<1>(*slot, NCOLS);
 }
 
+// ------------------------------------------------------------------ clusters
+// A pair of CTAs (cluster (2,1,1)) shares one tcgen05 MMA of M = 256: rank 0
+// (the leader) issues it, each CTA holds 128 rows of A, half of B's columns
+// and its 128 accumulator rows in its own TMEM.
+__device__ __forceinline__ int cluster_ctarank() { return static_cast<int>(dev::cluster_ctarank()); }
+__device__ __forceinline__ void cluster_sync() { dev::cluster_sync(); }
+
+// TMEM for a CTA pair: warp 0 of both CTAs allocates with cta_group::2 (the
+// same columns in both); released after a cluster barrier, so neither CTA
+// frees its columns while the leader's MMAs may still write them.
+template <int NCOLS>
+__device__ __forceinline__ void tmem_acquire2(u32 *slot) {
+  if (threadIdx.x / 32 == 0) {
+    tmem_alloc<2>(smem_u32(slot), NCOLS);
+    tmem_relinquish<2>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  dev::cluster_sync();  // both CTAs' semaphores are initialised before remote use
+  tc_fence_after();
+}
+
+template <int NCOLS>
+__device__ __forceinline__ void tmem_release2(u32 *slot) {
+  tc_fence_before();
+  __syncthreads();
+  dev::cluster_sync();
+  tc_fence_after();
+  if (threadIdx.x / 32 == 0) tmem_dealloc<2>(*slot, NCOLS);
+}
+
 template <class TT>
 __device__ __forceinline__ TT tensor_alloc(u32 slot, int col_offset) {
   TT t;
@@ -551,10 +582,48 @@ __device__ __forceinline__ void umma_abt(tt<float, M, N> &d, const st<T, M, K> &
   tc_commit(sem_addr(sem));
 }
 
+// 2-CTA forms (issued by the leader CTA of a pair): D (+)= A . B with
+// M = 256.  Each CTA passes its own tiles at the same shared offsets: A is
+// its 128 rows (128 x K), B its half of the columns (K x N/2); D is each
+// CTA's 128 x N accumulator.  `sem` is signalled in both CTAs.
+__device__ __forceinline__ void commit_pair(semaphore &sem) {
+  tc_commit2(mapa_cluster(sem_addr(sem), 0));
+  tc_commit2(mapa_cluster(sem_addr(sem), 1));
+}
+
+template <bool ACC, class T, int M, int N, int K, int KB, int NH>
+__device__ __forceinline__ void umma2_ab(tt<float, M, N> &d, const st<T, M, K> &a, const st<T, KB, NH> &b,
+                                         semaphore &sem) {
+  static_assert(KB == K && 2 * NH == N, "2-CTA tcgen05: B holds K x N/2 per CTA");
+  static_assert(M == 128, "2-CTA tcgen05: 128 rows per CTA (M = 256 per pair)");
+  static_assert(N % 32 == 0 && N >= 32 && N <= 256, "2-CTA tcgen05 N must be 32..256, a multiple of 32");
+  constexpr u32 idesc = make_idesc(umma_fmt<T>::v, umma_fmt<T>::v, false, true, 2 * M, N);
+#pragma unroll
+  for (int kk = 0; kk < K / 16; ++kk)
+    mma2_f16_ss(d.addr, desc_kmajor(a, kk), desc_mnmajor(b, kk), idesc, (ACC || kk > 0) ? 1u : 0u);
+  commit_pair(sem);
+}
+
+template <bool ACC, class T, int M, int N, int K, int NH, int KB>
+__device__ __forceinline__ void umma2_abt(tt<float, M, N> &d, const st<T, M, K> &a, const st<T, NH, KB> &b,
+                                          semaphore &sem) {
+  static_assert(KB == K && 2 * NH == N, "2-CTA tcgen05: B holds N/2 x K per CTA");
+  static_assert(M == 128, "2-CTA tcgen05: 128 rows per CTA (M = 256 per pair)");
+  static_assert(N % 32 == 0 && N >= 32 && N <= 256, "2-CTA tcgen05 N must be 32..256, a multiple of 32");
+  constexpr u32 idesc = make_idesc(umma_fmt<T>::v, umma_fmt<T>::v, false, false, 2 * M, N);
+#pragma unroll
+  for (int kk = 0; kk < K / 16; ++kk)
+    mma2_f16_ss(d.addr, desc_kmajor(a, kk), desc_kmajor(b, kk), idesc, (ACC || kk > 0) ? 1u : 0u);
+  commit_pair(sem);
+}
+
 template <int NCTA>
 __device__ __forceinline__ void tcgen05_commit(semaphore &sem) {
-  static_assert(NCTA == 1, "2-CTA commits need a cluster launch");
-  tc_commit(sem_addr(sem));
+  static_assert(NCTA == 1 || NCTA == 2, "tcgen05 commits span one CTA or a pair");
+  if constexpr (NCTA == 1)
+    tc_commit(sem_addr(sem));
+  else
+    commit_pair(sem);
 }
 
 __device__ __forceinline__ void tensor_load_wait() { tmem_wait_ld(); }
@@ -633,6 +702,101 @@ __device__ __forceinline__ void mma_AB_t(tt<float, M, N> &d, const st<T, M, K> &
   umma_abt<true>(d, a, b, sem);
 }
 
+template <class T, int M, int N, int K, int KB, int NH>
+__device__ __forceinline__ void mm2_AB(tt<float, M, N> &d, const st<T, M, K> &a, const st<T, KB, NH> &b,
+                                       semaphore &sem) {
+  umma2_ab<false>(d, a, b, sem);
+}
+template <class T, int M, int N, int K, int KB, int NH>
+__device__ __forceinline__ void mma2_AB(tt<float, M, N> &d, const st<T, M, K> &a, const st<T, KB, NH> &b,
+                                        semaphore &sem) {
+  umma2_ab<true>(d, a, b, sem);
+}
+template <class T, int M, int N, int K, int NH, int KB>
+__device__ __forceinline__ void mm2_ABt(tt<float, M, N> &d, const st<T, M, K> &a, const st<T, NH, KB> &b,
+                                        semaphore &sem) {
+  umma2_abt<false>(d, a, b, sem);
+}
+template <class T, int M, int N, int K, int NH, int KB>
+__device__ __forceinline__ void mma2_AB_t(tt<float, M, N> &d, const st<T, M, K> &a, const st<T, NH, KB> &b,
+                                          semaphore &sem) {
+  umma2_abt<true>(d, a, b, sem);
+}
+
+// TMEM -> shared without a register tile: thread i of warp w takes TMEM lane
+// 32 (w % 4) + i (accumulator row 32 (w % 4) + i), converts 32 columns at a
+// time and writes them as 16-byte pieces into the swizzled shared tile.
+// Ends with a proxy fence so a TMA store issued after the next barrier sees
+// the data.
+template <class TS, int SR_, int SC_, int M, int N>
+__device__ __forceinline__ void store(st<TS, SR_, SC_> &dst, const tt<float, M, N> &src) {
+  static_assert(sizeof(TS) == 2, "TMEM -> shared stores 16-bit tiles");
+  static_assert(SR_ == M && SC_ <= N && SC_ % 32 == 0, "shared tile must cover the accumulator rows");
+  using S = st<TS, SR_, SC_>;
+  const int row = warpid() * 32 + static_cast<int>(lane_id());
+  const u32 taddr = src.addr + (static_cast<u32>(warpid() * 32) << 16);
+  tc_fence_after();  // the MMAs' completion was observed through a semaphore
+#pragma unroll 1
+  for (int c0 = 0; c0 < SC_; c0 += 32) {
+    u32 v[32];
+    tmem_ld_32x32b_x32(taddr + c0, v);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      u32 w[4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h)
+        w[h] = pack2<TS>(__uint_as_float(v[8 * j + 2 * h]), __uint_as_float(v[8 * j + 2 * h + 1]));
+      *reinterpret_cast<uint4 *>(dst.raw + S::offset(row, c0 + 8 * j)) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+  fence_proxy_async_smem();
+}
+
+// TMEM -> global at tile coordinate `at` (tiles of the accumulator's M x N):
+// thread i of warp w writes accumulator row 32 (w % 4) + i, 16 bytes at a
+// time where the row and columns are in bounds and aligned, element by
+// element at a ragged edge.
+template <class TG, int GR, int GC, int M, int N>
+__device__ __forceinline__ void store(const gl<TG, GR, GC> &dst, const tt<float, M, N> &src, coord at) {
+  static_assert(sizeof(TG) == 2 || sizeof(TG) == 4, "TMEM -> global stores 16- or 32-bit elements");
+  static_assert(N % 32 == 0, "accumulator columns must be a multiple of 32");
+  const long long row = (long long)at.r * M + warpid() * 32 + static_cast<int>(lane_id());
+  const u32 taddr = src.addr + (static_cast<u32>(warpid() * 32) << 16);
+  tc_fence_after();
+#pragma unroll 1
+  for (int c0 = 0; c0 < N; c0 += 32) {
+    u32 v[32];
+    tmem_ld_32x32b_x32(taddr + c0, v);
+    tmem_wait_ld();
+    if (row >= (long long)dst.rows) continue;
+    const long long col0 = (long long)at.c * N + c0;
+    TG *p = dst.ptr + row * (long long)dst.cols + col0;
+    constexpr int PER = 16 / sizeof(TG);  // elements per 16-byte store
+    const bool vec = col0 + 32 <= (long long)dst.cols && ((reinterpret_cast<unsigned long long>(p) & 15) == 0) &&
+                     ((dst.cols * sizeof(TG)) % 16 == 0);
+#pragma unroll
+    for (int j = 0; j < 32 / PER; ++j) {
+      if (vec) {
+        u32 w[4];
+        if constexpr (sizeof(TG) == 2) {
+#pragma unroll
+          for (int h = 0; h < 4; ++h)
+            w[h] = pack2<TG>(__uint_as_float(v[8 * j + 2 * h]), __uint_as_float(v[8 * j + 2 * h + 1]));
+        } else {
+#pragma unroll
+          for (int h = 0; h < 4; ++h) w[h] = v[4 * j + h];
+        }
+        st_global_v4(p + PER * j, w[0], w[1], w[2], w[3]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < PER; ++e)
+          if (col0 + PER * j + e < (long long)dst.cols) p[PER * j + e] = from_f<TG>(__uint_as_float(v[PER * j + e]));
+      }
+    }
+  }
+}
+
 // TMEM -> registers: this warp's 32 TMEM lanes (quadrant warpid) become the
 // R = 32 rows of the register tile.  tcgen05.ld hands each thread one row;
 // shuffles move the values into mma fragment positions.
@@ -642,6 +806,7 @@ __device__ __forceinline__ void load_async(rt<T, R, C, 0> &dst, const tt<float, 
   const int lane = lane_id();
   const int g = lane >> 2, t = lane & 3;
   const u32 taddr = src.addr + (static_cast<u32>(warpid() * 32) << 16);
+  tc_fence_after();  // the MMAs' completion was observed through a semaphore
 #pragma unroll 1
   for (int c0 = 0; c0 < C; c0 += 32) {
     u32 row[32];
@@ -717,6 +882,32 @@ __device__ __forceinline__ void store_async(const gl<TG, GR, GC> &dst, const st<
 }
 
 __device__ __forceinline__ void store_async_read_wait() { bulk_wait_read<0>(); }
+
+// Loads into this CTA's shared tile whose bytes are counted on `sem` of
+// cluster CTA `dst_cta` (the pair leader's copy, for a 2-CTA MMA).  The
+// leader expects both CTAs' bytes (expect_bytes on its own semaphore).  No
+// multicast: every CTA fetches its own tiles.
+namespace cluster {
+__device__ __forceinline__ void expect_bytes(semaphore &s, int bytes) {
+  mbar_arrive_expect_tx(sem_addr(s), static_cast<u32>(bytes));
+}
+
+template <class T, int R, int C, class TG, int GR, int GC>
+__device__ __forceinline__ void load_async(st<T, R, C> &dst, const gl<TG, GR, GC> &src, coord at,
+                                           semaphore &sem, int dst_cta) {
+  using S = st<T, R, C>;
+  static_assert(GR == R && GC == C, "TMA box (global tile shape) differs from the shared tile");
+  static_assert(sizeof(T) == sizeof(TG), "shared and global element sizes differ");
+  constexpr int BOX_R = R < 256 ? R : 256;
+  const u32 bar = mapa_cluster(sem_addr(sem), static_cast<u32>(dst_cta));
+#pragma unroll
+  for (int ch = 0; ch < S::NCH; ++ch)
+#pragma unroll
+    for (int r0 = 0; r0 < R; r0 += BOX_R)
+      tma_load_2d_pair(dst.base() + ch * S::CHB + r0 * S::ROWB, &src.tmap, bar, at.c * C + ch * S::CC,
+                       at.r * R + r0);
+}
+}  // namespace cluster
 
 }  // namespace tma
 

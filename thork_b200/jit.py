@@ -97,15 +97,23 @@ class JittedKernel:
 
     # -- launching
     def __getitem__(self, dispatch_spec) -> "_Launcher":
-        if not (isinstance(dispatch_spec, tuple) and len(dispatch_spec) == 2):
+        """``kernel[grid, block]``, or ``kernel[grid, block, cluster]`` for a
+        thread-block-cluster launch (2-CTA tile kernels use ``(2, 1, 1)``)."""
+        if not (isinstance(dispatch_spec, tuple) and len(dispatch_spec) in (2, 3)):
             raise TypeError(
                 f"Kernel must be subscripted with (grid_size, block_size), got {dispatch_spec!r}")
-        grid, block = dispatch_spec
-        return _Launcher(self, grid, block)
+        return _Launcher(self, *dispatch_spec)
 
-    def bind(self, grid, block) -> "BoundKernel":
-        """A callable with ``grid``/``block`` baked in."""
-        return BoundKernel(self, grid, block)
+    def bind(self, grid, block, cluster=None) -> "BoundKernel":
+        """A callable with ``grid``/``block`` (and ``cluster``) baked in."""
+        return BoundKernel(self, grid, block, cluster)
+
+    @property
+    def cluster_ctas(self) -> int:
+        """CTAs per cluster the kernel's tile operations need (2 for
+        cluster-pair tensor-core operations, else 1)."""
+        self._ensure_traced()
+        return int(getattr(self._builder, "tk_cluster", 1))
 
     def compile_for_arch(self, arch: str) -> None:
         """Trace and compile (NVRTC, no launch) for ``arch``; only sm_100a
@@ -142,19 +150,28 @@ def _dims(v) -> tuple:
 
 
 class _Launcher:
-    __slots__ = ("_kernel", "_grid", "_block")
+    __slots__ = ("_kernel", "_grid", "_block", "_cluster")
 
-    def __init__(self, kernel: JittedKernel, grid, block):
+    def __init__(self, kernel: JittedKernel, grid, block, cluster=None):
         self._kernel = kernel
         self._grid = _dims(grid)
         self._block = _dims(block)
+        self._cluster = _dims(cluster) if cluster is not None else None
 
     def __call__(self, *args):
         k = self._kernel
+        need = k.cluster_ctas  # traces the kernel; checked before any compile or launch
+        cl = self._cluster or (1, 1, 1)
+        if need > 1 and cl != (need, 1, 1):
+            raise ValueError(
+                f"Kernel '{k.name}' uses cluster-pair tile operations; launch it as "
+                f"kernel[grid, block, ({need}, 1, 1)] (got cluster {cl})")
+        if cl[0] * cl[1] * cl[2] > 1 and any(g % c for g, c in zip(self._grid, cl)):
+            raise ValueError(f"grid {self._grid} is not a multiple of the cluster {cl}")
         k._ensure_compiled()
         runtime.dispatch(k._func, k._builder.params, args, self._grid, self._block,
                          shared_mem_bytes=k.dynamic_smem, uses_status=k._builder.uses_status,
-                         name=k.name)
+                         name=k.name, cluster=self._cluster)
 
 
 def jit(fn: Callable) -> JittedKernel:
@@ -167,15 +184,19 @@ class BoundKernel:
     """A JittedKernel with grid and block bound; call it with the pointer and
     constant arguments."""
 
-    __slots__ = ("_kernel", "_grid", "_block")
+    __slots__ = ("_kernel", "_grid", "_block", "_cluster")
 
-    def __init__(self, kernel, grid, block):
+    def __init__(self, kernel, grid, block, cluster=None):
         self._kernel = kernel
         self._grid = tuple(int(x) for x in grid)
         self._block = tuple(int(x) for x in block)
+        self._cluster = tuple(int(x) for x in cluster) if cluster is not None else None
 
     def __call__(self, *args):
-        self._kernel[self._grid, self._block](*args)
+        if self._cluster is None:
+            self._kernel[self._grid, self._block](*args)
+        else:
+            self._kernel[self._grid, self._block, self._cluster](*args)
 
     @property
     def cuda_source(self) -> str:

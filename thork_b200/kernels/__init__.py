@@ -6,9 +6,13 @@
 
     add = tk.kernels.matrix_add((1024, 1024))
     add(C, A, B)
+
+    tm = tk.kernels.tile_matmul(4096, 4096, 4096, ncta=2)   # written in tk.kittens
+    tm(C, A, B)
 """
 
 from .matmul import matmul
 from .matrix_add import matrix_add
+from .tile_matmul import tile_matmul
 
-__all__ = ["matmul", "matrix_add"]
+__all__ = ["matmul", "matrix_add", "tile_matmul"]

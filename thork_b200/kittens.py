@@ -32,6 +32,7 @@ __all__ = [
     "swap_layout", "mma_AB", "mma_AB_t", "warpgroup", "Semaphore", "semaphore",
     "init_semaphore", "wait", "tma", "TensorTile", "TensorAllocator", "tt_bf", "tt_hf",
     "tt_fl", "tensor_allocator", "tensor_alloc", "tcgen05_commit", "tensor_load_wait",
+    "cluster_ctarank", "cluster_sync",
 ]
 
 _ELEM = {"float32": "float", "float16": "__half", "bfloat16": "__nv_bfloat16",
@@ -72,6 +73,14 @@ def mark_kittens(b: KernelBuilder) -> None:
         b.tk_smem_bytes = 0
         b.tk_min_smem = 0
         b.tk_epilogue = []
+        b.tk_cluster = 1
+
+
+def _mark_pair(b: KernelBuilder) -> None:
+    """The kernel uses 2-CTA (cluster pair) operations: it must be launched
+    with a cluster of (2, 1, 1)."""
+    mark_kittens(b)
+    b.tk_cluster = 2
 
 
 def _mark_tma(b: KernelBuilder) -> None:
@@ -140,18 +149,20 @@ class SharedTile(_Handle):
 
 
 class TensorTile(_Handle):
-    __slots__ = ("_rows", "_cols")
+    __slots__ = ("_rows", "_cols", "_ncta")
 
     def __init__(self, expr, dtype, builder, rows, cols):
         super().__init__(expr, dtype, builder)
         self._rows, self._cols = rows, cols
+        self._ncta = 1  # 2 once bound to a cluster-pair allocator
 
 
 class TensorAllocator(_Handle):
-    __slots__ = ()
+    __slots__ = ("_ncta",)
 
-    def __init__(self, name: str, builder: KernelBuilder):
+    def __init__(self, name: str, builder: KernelBuilder, ncta: int = 1):
         super().__init__(ir.Name(name), dt.uint32, builder)
+        self._ncta = ncta
 
 
 class Semaphore(_Handle):
@@ -234,13 +245,16 @@ tt_fl = _tt_factory("tt_fl", dt.float32)
 def tensor_allocator(nblocks_per_sm: int = 1, ncta: int = 1) -> TensorAllocator:
     """Allocate this CTA's share of tensor memory (512 / nblocks_per_sm
     columns); it is released when the kernel finishes.  Must be reached by
-    every thread of the block (top level of the kernel)."""
+    every thread of the block (top level of the kernel).
+
+    ``ncta=2`` allocates for a CTA pair (``tcgen05.alloc.cta_group::2`` in
+    both CTAs): the kernel must then be launched with a cluster of
+    ``(2, 1, 1)`` (``kernel[grid, block, (2, 1, 1)]``), tiles bound to this
+    allocator take the 2-CTA MMA forms, and the allocation also serves as the
+    cluster barrier that makes both CTAs' semaphores visible to each other
+    (initialise them before it)."""
     if nblocks_per_sm not in (1, 2) or ncta not in (1, 2):
         raise ValueError("tensor_allocator: nblocks_per_sm and ncta must each be 1 or 2")
-    if ncta != 1:
-        raise NotImplementedError(
-            "tensor_allocator(ncta=2) needs a 2-CTA cluster launch, which kernel[grid, block] "
-            "cannot express; the 2-CTA path is the library GEMM (tk.kernels.matmul)")
     b = current_builder()
     mark_kittens(b)
     name = b.fresh_name("tm")
@@ -250,9 +264,14 @@ def tensor_allocator(nblocks_per_sm: int = 1, ncta: int = 1) -> TensorAllocator:
     # further CTA off the SM, so allocations never contend.
     b.tk_min_smem = max(b.tk_min_smem, (120 if nblocks_per_sm == 1 else 80) * 1024)
     b.add_stmt(ir.Decl(name, "unsigned int", qual="__shared__"))
-    _stmt(b, f"{NS}::tmem_acquire<{cols}>", [ir.Verbatim(f"&{name}")])
-    b.tk_epilogue.append(f"{NS}::tmem_release<{cols}>(&{name});")
-    return TensorAllocator(name, b)
+    if ncta == 2:
+        _mark_pair(b)
+        _stmt(b, f"{NS}::tmem_acquire2<{cols}>", [ir.Verbatim(f"&{name}")])
+        b.tk_epilogue.append(f"{NS}::tmem_release2<{cols}>(&{name});")
+    else:
+        _stmt(b, f"{NS}::tmem_acquire<{cols}>", [ir.Verbatim(f"&{name}")])
+        b.tk_epilogue.append(f"{NS}::tmem_release<{cols}>(&{name});")
+    return TensorAllocator(name, b, ncta)
 
 
 def tensor_alloc(tt: TensorTile, alloc: TensorAllocator, col_offset=0) -> None:
@@ -264,6 +283,7 @@ def tensor_alloc(tt: TensorTile, alloc: TensorAllocator, col_offset=0) -> None:
         raise TypeError("tensor_alloc alloc must be a TensorAllocator")
     b = current_builder()
     mark_kittens(b)
+    tt._ncta = alloc._ncta
     b.add_stmt(ir.AssignStmt(tt._expr.name, "=", ir.CallExpr(
         f"{NS}::tensor_alloc", [alloc._expr, to_expr(col_offset)],
         [f"decltype({tt._expr.name})"])))
@@ -271,16 +291,36 @@ def tensor_alloc(tt: TensorTile, alloc: TensorAllocator, col_offset=0) -> None:
 
 def tcgen05_commit(sem: Semaphore, ncta: int = 1) -> None:
     """Arrive on ``sem`` once every tcgen05 op issued so far by this thread
-    has completed (issue from the thread that issued the MMAs)."""
+    has completed (issue from the thread that issued the MMAs).  With
+    ``ncta=2`` (the pair leader's MMA thread) the arrival lands on ``sem`` in
+    both CTAs of the pair."""
     if not isinstance(sem, Semaphore):
         raise TypeError("tcgen05_commit sem must be a Semaphore")
     if ncta not in (1, 2):
         raise ValueError("tcgen05_commit ncta must be 1 or 2")
-    if ncta != 1:
-        raise NotImplementedError("tcgen05_commit(ncta=2) needs a 2-CTA cluster launch")
+    b = current_builder()
+    if ncta == 2:
+        _mark_pair(b)
+    else:
+        mark_kittens(b)
+    _stmt(b, f"{NS}::tcgen05_commit<{ncta}>", [sem._expr])
+
+
+def cluster_ctarank() -> Value:
+    """This CTA's rank in its cluster (0 or 1 for a pair; 0 without a
+    cluster launch)."""
     b = current_builder()
     mark_kittens(b)
-    _stmt(b, f"{NS}::tcgen05_commit<{ncta}>", [sem._expr])
+    name = b.fresh_name("ctarank")
+    b.add_stmt(ir.Decl(name, "int", init=ir.CallExpr(f"{NS}::cluster_ctarank")))
+    return Value(ir.Name(name), dt.int32)
+
+
+def cluster_sync() -> None:
+    """Barrier over every thread of every CTA in the cluster."""
+    b = current_builder()
+    mark_kittens(b)
+    _stmt(b, f"{NS}::cluster_sync", [])
 
 
 def tensor_load_wait() -> None:
@@ -380,6 +420,17 @@ def _store(scope: str, dst, src, coord) -> None:
     if isinstance(dst, GlobalHandle):
         if coord is None:
             raise TypeError("store(global, tile, coord) requires a coord tuple")
+        if isinstance(src, TensorTile):
+            # tensor memory -> global, one accumulator row per thread of the group
+            if scope != "warpgroup":
+                raise TypeError("store(global, tensor) is a warpgroup operation")
+            if dst._dtype.nbytes not in (2, 4) or src._cols % 32:
+                raise TypeError("store(global, tensor): 16- or 32-bit global, accumulator columns "
+                                "a multiple of 32")
+            b.mark_written(dst._expr, kinds=("kittens_global",))
+            _stmt(b, f"{NS}::{scope}::store", [dst._expr, src._expr, _coord(coord)])
+            _hook("store", dst, src, coord)
+            return
         if not isinstance(src, (RegisterTile, SharedTile)):
             raise TypeError(f"kittens.store: cannot store a {type(src).__name__} to global memory")
         if isinstance(src, SharedTile):
@@ -393,6 +444,16 @@ def _store(scope: str, dst, src, coord) -> None:
             raise TypeError("store(shared, register) does not take a coord")
         if src._layout != "row":
             raise TypeError("store(shared, register) needs a row-layout register tile")
+        _stmt(b, f"{NS}::{scope}::store", [dst._expr, src._expr])
+    elif isinstance(dst, SharedTile) and isinstance(src, TensorTile):
+        # tensor memory -> shared, one accumulator row per thread of the group
+        if scope != "warpgroup" or coord is not None:
+            raise TypeError("store(shared, tensor) is a warpgroup operation without a coord")
+        if dst._dtype.nbytes != 2 or dst._rows != src._rows or dst._cols > src._cols \
+                or dst._cols % 32:
+            raise TypeError(
+                f"store(shared, tensor): a 16-bit shared tile of the accumulator's {src._rows} rows "
+                f"and a multiple of 32 columns up to {src._cols}, got ({dst._rows}, {dst._cols})")
         _stmt(b, f"{NS}::{scope}::store", [dst._expr, src._expr])
     else:
         raise TypeError(
@@ -429,7 +490,10 @@ def _mma(scope: str, func: str, *args) -> None:
     _hook(func, c, a, bt, c_in)
 
 
-def _tcgen05(func: str, d, a, bt, sem) -> None:
+_PAIR_FORMS = {"mm_AB": "mm2_AB", "mma_AB": "mma2_AB", "mma_AB_t": "mma2_AB_t", "mm_ABt": "mm2_ABt"}
+
+
+def _tcgen05(func: str, d, a, bt, sem, ncta=None) -> None:
     if not isinstance(d, TensorTile):
         raise TypeError(f"warpgroup.{func} (tcgen05) d must be a TensorTile")
     if not isinstance(a, SharedTile):
@@ -438,10 +502,19 @@ def _tcgen05(func: str, d, a, bt, sem) -> None:
         raise TypeError(f"warpgroup.{func} (tcgen05) b must be a SharedTile")
     if not isinstance(sem, Semaphore):
         raise TypeError(f"warpgroup.{func} (tcgen05) sem must be a Semaphore")
+    pair = (ncta or d._ncta) == 2
     b = current_builder()
+    if pair:
+        # D's tensor memory must come from a pair allocator; B holds half the
+        # columns of D in each CTA
+        if d._ncta != 2:
+            raise TypeError(f"warpgroup.{_PAIR_FORMS[func]} needs a TensorTile bound to "
+                            "tensor_allocator(ncta=2)")
+        _mark_pair(b)
+        _stmt(b, f"{NS}::warpgroup::{_PAIR_FORMS[func]}", [d._expr, a._expr, bt._expr, sem._expr])
+        return
     mark_kittens(b)
-    name = {"mm_AB": "mm_AB", "mma_AB": "mma_AB", "mma_AB_t": "mma_AB_t", "mm_ABt": "mm_ABt"}[func]
-    _stmt(b, f"{NS}::warpgroup::{name}", [d._expr, a._expr, bt._expr, sem._expr])
+    _stmt(b, f"{NS}::warpgroup::{func}", [d._expr, a._expr, bt._expr, sem._expr])
 
 
 def zero(rt: RegisterTile) -> None:
@@ -526,6 +599,29 @@ class _WarpgroupNS:
         _tcgen05("mm_ABt", d, a, b, sem)
 
     @staticmethod
+    def mm2_AB(d, a, b, sem):
+        """2-CTA tcgen05 ``d = a @ b`` (M = 256 over the pair), issued by the
+        pair leader: ``a`` is each CTA's 128 x K rows, ``b`` its K x N/2
+        columns, ``d`` each CTA's 128 x N accumulator; ``sem`` is signalled
+        in both CTAs once the operands have been consumed."""
+        _tcgen05("mm_AB", d, a, b, sem, ncta=2)
+
+    @staticmethod
+    def mma2_AB(d, a, b, sem):
+        """2-CTA tcgen05 ``d += a @ b`` (see ``mm2_AB``)."""
+        _tcgen05("mma_AB", d, a, b, sem, ncta=2)
+
+    @staticmethod
+    def mm2_ABt(d, a, b, sem):
+        """2-CTA tcgen05 ``d = a @ b^T`` with ``b`` N/2 x K per CTA."""
+        _tcgen05("mm_ABt", d, a, b, sem, ncta=2)
+
+    @staticmethod
+    def mma2_AB_t(d, a, b, sem):
+        """2-CTA tcgen05 ``d += a @ b^T`` with ``b`` N/2 x K per CTA."""
+        _tcgen05("mma_AB_t", d, a, b, sem, ncta=2)
+
+    @staticmethod
     def load_async(dst, src):
         """Tensor memory -> registers: this warp's 32 TMEM lanes into a
         32-row register tile."""
@@ -601,6 +697,43 @@ class _TmaNS:
         b = current_builder()
         _mark_tma(b)
         _stmt(b, f"{NS}::tma::store_async_read_wait", [])
+
+
+class _TmaClusterNS:
+    """TMA loads for a CTA pair: each CTA fetches its own tiles into its own
+    shared memory (there is no multicast form), and the bytes are counted on
+    a semaphore of the CTA ``dst_cta`` — the pair leader, whose MMA reads
+    both CTAs' tiles."""
+
+    @staticmethod
+    def expect_bytes(sem: Semaphore, n_bytes) -> None:
+        """Arrive on this CTA's ``sem`` and expect ``n_bytes`` (both CTAs'
+        loads, when it is the leader's)."""
+        if not isinstance(sem, Semaphore):
+            raise TypeError("tma.cluster.expect_bytes expects a Semaphore")
+        b = current_builder()
+        _mark_tma(b)
+        _mark_pair(b)
+        _stmt(b, f"{NS}::tma::cluster::expect_bytes", [sem._expr, to_expr(n_bytes)])
+
+    @staticmethod
+    def load_async(dst: SharedTile, src: GlobalHandle, coord: tuple, sem: Semaphore,
+                   dst_cta=0) -> None:
+        if not isinstance(dst, SharedTile):
+            raise TypeError("tma.cluster.load_async dst must be a SharedTile")
+        if not isinstance(src, GlobalHandle):
+            raise TypeError("tma.cluster.load_async src must be a kittens.Global parameter")
+        if not isinstance(sem, Semaphore):
+            raise TypeError("tma.cluster.load_async sem must be a Semaphore")
+        _check_tma(dst, src)
+        b = current_builder()
+        _mark_tma(b)
+        _mark_pair(b)
+        _stmt(b, f"{NS}::tma::cluster::load_async",
+              [dst._expr, src._expr, _coord(coord), sem._expr, to_expr(dst_cta)])
+
+
+_TmaNS.cluster = _TmaClusterNS()
 
 
 def _check_tma(tile: SharedTile, glob: GlobalHandle) -> None:

@@ -806,7 +806,7 @@ def pack_global(ptr: int, rows: int, cols: int, param: ir.Param):
 
 def dispatch(func: int, params: Sequence[ir.Param], user_args: Sequence, grid_size, block_size,
              shared_mem_bytes: int = 0, stream: int = 0, *, uses_status: bool = False,
-             name: str = "kernel") -> None:
+             name: str = "kernel", cluster=None) -> None:
     """Copy NumPy arguments in, launch, synchronise, copy written buffers back.
 
     DeviceArray arguments are used in place (no copies).  Only parameters the
@@ -843,7 +843,8 @@ def dispatch(func: int, params: Sequence[ir.Param], user_args: Sequence, grid_si
                 storage.append(_scalar_storage(a, p))
         if uses_status:
             storage.append(ctypes.c_void_p(status_pointer()))
-        launch(func, grid_size, block_size, storage, smem=shared_mem_bytes, stream=s)
+        launch(func, grid_size, block_size, storage, smem=shared_mem_bytes, stream=s,
+               cluster=cluster)
         for arr, ptr in copies_back:
             copy_dtoh(arr, ptr, s, sync=False)
         s.synchronize()
