@@ -1029,23 +1029,33 @@ def check_gemm_rows(D, A, B, rt, nrows=CHECK_ROWS):
             "pass": err <= TOL}
 
 
-def time_traced(launch, args, rt, flops, peaks, note, reps=20):
-    """Device time of a traced launch: CUDA events on the stream the drop-in
-    call launches on, around each (synchronous) call."""
-    s = rt._dispatch_stream()
-    times = []
+def time_traced(launch, args, rt, flops, peaks, note, reps=50):
+    """Device time of a traced kernel: its device-resident arguments packed
+    once (``prepare``), ``reps`` launches queued back to back on one stream,
+    CUDA events around them.  The synchronous drop-in call (argument packing,
+    launch, synchronise) is timed beside it on the host."""
+    s = rt.Stream()
+    prepared = launch.prepare(*args)
+    for _ in range(5):
+        prepared.launch(s)
+    s.synchronize()
+    e0, e1 = rt.Event(), rt.Event()
+    e0.record(s)
     for _ in range(reps):
-        e0, e1 = rt.Event(), rt.Event()
-        e0.record(s)
+        prepared.launch(s)
+    e1.record(s)
+    e1.synchronize()
+    ms = e0.elapsed_ms(e1) / reps
+    t0 = time.perf_counter()
+    for _ in range(5):
         launch(*args)
-        e1.record(s)
-        e1.synchronize()
-        times.append(e0.elapsed_ms(e1))
-    ms = statistics.median(times)
+    call_ms = (time.perf_counter() - t0) / 5 * 1e3
     tf = flops / (ms * 1e-3) / 1e12
     return {"TFLOP/s": round(tf, 1), "ms": round(ms, 4),
             "frac_of_peak": round(tf / peaks["bf16_tflops"], 3), "note": note,
-            "timing": "median of CUDA-event device times around each drop-in launch"}
+            "timing": f"{reps} prepared launches back to back, CUDA events",
+            "dropin_call_ms": round(call_ms, 4),
+            "status": rt.kernel_status()}
 
 
 def traffic_from_profiles(workload):

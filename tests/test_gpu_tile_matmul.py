@@ -72,3 +72,26 @@ def test_pair_and_single_cta_agree_bit_for_bit():
     tk.kernels.tile_matmul(m, n, k, ncta=1)(c1, a16, b16)
     tk.kernels.tile_matmul(m, n, k, ncta=2)(c2, a16, b16)
     np.testing.assert_array_equal(c1, c2)
+
+
+def test_prepared_launches_match_dropin_call():
+    """Arguments packed once, launches queued asynchronously on a stream,
+    give the same bits as the synchronous drop-in call; host arrays are
+    refused (a prepared launch copies nothing)."""
+    rt = tk.runtime
+    m, n, k = 256, 512, 512
+    _, _, a16, b16 = _inputs(m, n, k, seed=9, scale=1.0)
+    mm = tk.kernels.tile_matmul(m, n, k, ncta=2)
+    want = np.zeros((m, n), np.uint16)
+    mm(want, a16, b16)
+    A, B, C = rt.to_device(a16), rt.to_device(b16), rt.empty((m, n), np.uint16)
+    C.zero()
+    s = rt.Stream()
+    prepared = mm.prepare(C, A, B)
+    for _ in range(3):
+        prepared.launch(s)
+    s.synchronize()
+    np.testing.assert_array_equal(C.to_host(), want)
+    assert rt.kernel_status() == 0
+    with pytest.raises(TypeError, match="DeviceArray"):
+        mm.prepare(want, A, B)

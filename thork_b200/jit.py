@@ -150,13 +150,23 @@ def _dims(v) -> tuple:
 
 
 class _Launcher:
-    __slots__ = ("_kernel", "_grid", "_block", "_cluster")
+    __slots__ = ("_kernel", "_grid", "_block", "_cluster", "_prepare")
 
     def __init__(self, kernel: JittedKernel, grid, block, cluster=None):
         self._kernel = kernel
         self._grid = _dims(grid)
         self._block = _dims(block)
         self._cluster = _dims(cluster) if cluster is not None else None
+        self._prepare = False
+
+    def prepare(self, *args) -> "runtime.PreparedLaunch":
+        """Pack device-resident arguments once; ``.launch(stream)`` then queues
+        the kernel asynchronously (no copies, no synchronisation)."""
+        self._prepare = True
+        try:
+            return self(*args)
+        finally:
+            self._prepare = False
 
     def __call__(self, *args):
         k = self._kernel
@@ -169,6 +179,10 @@ class _Launcher:
         if cl[0] * cl[1] * cl[2] > 1 and any(g % c for g, c in zip(self._grid, cl)):
             raise ValueError(f"grid {self._grid} is not a multiple of the cluster {cl}")
         k._ensure_compiled()
+        if getattr(self, "_prepare", False):
+            return runtime.PreparedLaunch(k._func, k._builder.params, args, self._grid, self._block,
+                                          k.dynamic_smem, uses_status=k._builder.uses_status,
+                                          cluster=self._cluster)
         runtime.dispatch(k._func, k._builder.params, args, self._grid, self._block,
                          shared_mem_bytes=k.dynamic_smem, uses_status=k._builder.uses_status,
                          name=k.name, cluster=self._cluster)
@@ -192,11 +206,18 @@ class BoundKernel:
         self._block = tuple(int(x) for x in block)
         self._cluster = tuple(int(x) for x in cluster) if cluster is not None else None
 
-    def __call__(self, *args):
+    def _launcher(self) -> "_Launcher":
         if self._cluster is None:
-            self._kernel[self._grid, self._block](*args)
-        else:
-            self._kernel[self._grid, self._block, self._cluster](*args)
+            return self._kernel[self._grid, self._block]
+        return self._kernel[self._grid, self._block, self._cluster]
+
+    def __call__(self, *args):
+        self._launcher()(*args)
+
+    def prepare(self, *args) -> "runtime.PreparedLaunch":
+        """See ``_Launcher.prepare``: device-resident arguments packed once
+        for asynchronous launches."""
+        return self._launcher().prepare(*args)
 
     @property
     def cuda_source(self) -> str:

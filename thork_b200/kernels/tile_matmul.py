@@ -209,6 +209,11 @@ class _TileMatmul:
     def __call__(self, C, A, B):
         self.kernel(A, B, C, self._k, self._n)
 
+    def prepare(self, C, A, B):
+        """Device arrays packed once; ``.launch(stream)`` queues the kernel
+        without synchronising (``runtime.PreparedLaunch``)."""
+        return self.kernel.prepare(A, B, C, self._k, self._n)
+
     @property
     def cuda_source(self) -> str:
         return self.kernel.cuda_source

@@ -853,3 +853,53 @@ def dispatch(func: int, params: Sequence[ir.Param], user_args: Sequence, grid_si
     finally:
         for b in owned:
             b.free()
+
+
+class PreparedLaunch:
+    """A traced kernel with its arguments packed once, for repeated
+    asynchronous launches on device-resident data (for example back-to-back
+    launches timed with events, or a launch sequence without Python argument
+    handling in between).
+
+    Every pointer / global argument must be a ``DeviceArray`` (nothing is
+    copied in or back).  ``launch(stream)`` queues the kernel and returns at
+    once; a kernel with bounded waits reports to the device status word, read
+    with ``kernel_status()`` after synchronising.  No reference counterpart:
+    the reference's launches always copy and synchronise
+    (``runtime.py:656-700``)."""
+
+    def __init__(self, func: int, params: Sequence[ir.Param], user_args: Sequence, grid_size,
+                 block_size, shared_mem_bytes: int = 0, *, uses_status: bool = False,
+                 cluster=None):
+        get_device()
+        bindable = [p for p in params if p.bindable]
+        if len(user_args) != len(bindable):
+            raise TypeError(
+                f"Kernel expected {len(bindable)} arguments (pointer + constant + kittens_global "
+                f"params), got {len(user_args)}")
+        storage = []
+        for p, a in zip(bindable, user_args):
+            if p.kind in ("pointer", "kittens_global"):
+                if not isinstance(a, DeviceArray):
+                    raise TypeError(f"prepared launches take DeviceArray arguments; parameter "
+                                    f"'{p.name}' got {type(a).__name__}")
+                arr = _expect_pointer_arg(a, p) if p.kind == "pointer" else _expect_kittens_arg(a, p)
+                storage.append(ctypes.c_void_p(arr.ptr) if p.kind == "pointer"
+                               else pack_global(arr.ptr, arr.shape[0], arr.shape[1], p))
+            else:
+                storage.append(_scalar_storage(a, p))
+        if uses_status:
+            storage.append(ctypes.c_void_p(status_pointer()))
+        self._storage = storage  # keeps the argument bytes alive
+        n = len(storage)
+        self._ptrs = (ctypes.c_void_p * max(n, 1))(
+            *[ctypes.cast(ctypes.pointer(a), ctypes.c_void_p) for a in storage])
+        self._grid = (ctypes.c_uint * 3)(*[int(x) for x in grid_size])
+        self._block = (ctypes.c_uint * 3)(*[int(x) for x in block_size])
+        self._cluster = (ctypes.c_uint * 3)(*[int(x) for x in cluster]) if cluster else None
+        self._func = func
+        self._smem = int(shared_mem_bytes)
+
+    def launch(self, stream: Optional[Stream] = None) -> None:
+        check(lib().thork_launch(self._func, self._grid, self._block, self._cluster, self._smem,
+                                 stream.handle if stream else None, self._ptrs), "launch")
