@@ -887,7 +887,7 @@ __device__ __forceinline__ void store_async_read_wait() { bulk_wait_read<0>(); }
 // cluster CTA `dst_cta` (the pair leader's copy, for a 2-CTA MMA).  The
 // leader expects both CTAs' bytes (expect_bytes on its own semaphore).  No
 // multicast: every CTA fetches its own tiles.
-namespace cluster {
+namespace pair {
 __device__ __forceinline__ void expect_bytes(semaphore &s, int bytes) {
   mbar_arrive_expect_tx(sem_addr(s), static_cast<u32>(bytes));
 }
@@ -907,7 +907,7 @@ __device__ __forceinline__ void load_async(st<T, R, C> &dst, const gl<TG, GR, GC
       tma_load_2d_pair(dst.base() + ch * S::CHB + r0 * S::ROWB, &src.tmap, bar, at.c * C + ch * S::CC,
                        at.r * R + r0);
 }
-}  // namespace cluster
+}  // namespace pair
 
 }  // namespace tma
 

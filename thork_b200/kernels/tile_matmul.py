@@ -17,7 +17,7 @@ same ``tk.kittens`` vocabulary, arranged as a warp-specialised pipeline:
 ``ncta=1``: one CTA per 128 x 256 output tile, 4 stages of 48 KiB.
 ``ncta=2``: a cluster pair per 256 x 256 tile (``tcgen05.mma.cta_group::2``):
 each CTA loads its 128 rows of A and 128 columns of B into its own shared
-memory (no multicast), both CTAs' loads count on the leader's ``full``
+memory (each CTA issues its own loads), both CTAs' loads count on the leader's ``full``
 semaphore, the leader issues the MMA and its commits land in both CTAs;
 6 stages of 32 KiB per CTA.
 
@@ -155,9 +155,9 @@ def _two_cta(M: int, N: int, K: int, stages: int = 6) -> BoundKernel:
                         with if_(kb < nkb):
                             kt.wait(empty[s], ph ^ 1)
                             with if_(rank == 0):
-                                kt.tma.cluster.expect_bytes(full[s], pair_bytes)
-                            kt.tma.cluster.load_async(a_s[s], A, (2 * bm + rank, kb), full[s], 0)
-                            kt.tma.cluster.load_async(b_s[s], B, (kb, 2 * bn + rank), full[s], 0)
+                                kt.tma.pair.expect_bytes(full[s], pair_bytes)
+                            kt.tma.pair.load_async(a_s[s], A, (2 * bm + rank, kb), full[s], 0)
+                            kt.tma.pair.load_async(b_s[s], B, (kb, 2 * bn + rank), full[s], 0)
                     ph ^= 1
         with if_(warp == 1):
             with if_((lane == 0) & (rank == 0)):

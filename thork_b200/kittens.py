@@ -699,9 +699,9 @@ class _TmaNS:
         _stmt(b, f"{NS}::tma::store_async_read_wait", [])
 
 
-class _TmaClusterNS:
+class _TmaPairNS:
     """TMA loads for a CTA pair: each CTA fetches its own tiles into its own
-    shared memory (there is no multicast form), and the bytes are counted on
+    shared memory (no load is shared between CTAs), and the bytes are counted on
     a semaphore of the CTA ``dst_cta`` — the pair leader, whose MMA reads
     both CTAs' tiles."""
 
@@ -710,30 +710,30 @@ class _TmaClusterNS:
         """Arrive on this CTA's ``sem`` and expect ``n_bytes`` (both CTAs'
         loads, when it is the leader's)."""
         if not isinstance(sem, Semaphore):
-            raise TypeError("tma.cluster.expect_bytes expects a Semaphore")
+            raise TypeError("tma.pair.expect_bytes expects a Semaphore")
         b = current_builder()
         _mark_tma(b)
         _mark_pair(b)
-        _stmt(b, f"{NS}::tma::cluster::expect_bytes", [sem._expr, to_expr(n_bytes)])
+        _stmt(b, f"{NS}::tma::pair::expect_bytes", [sem._expr, to_expr(n_bytes)])
 
     @staticmethod
     def load_async(dst: SharedTile, src: GlobalHandle, coord: tuple, sem: Semaphore,
                    dst_cta=0) -> None:
         if not isinstance(dst, SharedTile):
-            raise TypeError("tma.cluster.load_async dst must be a SharedTile")
+            raise TypeError("tma.pair.load_async dst must be a SharedTile")
         if not isinstance(src, GlobalHandle):
-            raise TypeError("tma.cluster.load_async src must be a kittens.Global parameter")
+            raise TypeError("tma.pair.load_async src must be a kittens.Global parameter")
         if not isinstance(sem, Semaphore):
-            raise TypeError("tma.cluster.load_async sem must be a Semaphore")
+            raise TypeError("tma.pair.load_async sem must be a Semaphore")
         _check_tma(dst, src)
         b = current_builder()
         _mark_tma(b)
         _mark_pair(b)
-        _stmt(b, f"{NS}::tma::cluster::load_async",
+        _stmt(b, f"{NS}::tma::pair::load_async",
               [dst._expr, src._expr, _coord(coord), sem._expr, to_expr(dst_cta)])
 
 
-_TmaNS.cluster = _TmaClusterNS()
+_TmaNS.pair = _TmaPairNS()
 
 
 def _check_tma(tile: SharedTile, glob: GlobalHandle) -> None:
