@@ -23,5 +23,10 @@ os.environ.setdefault("THORK_CACHE_DIR", os.path.join(_SCRATCH, "nvrtc_cache"))
 tempfile.tempdir = os.path.join(_SCRATCH, "tmp")
 
 
+# byte-for-byte copies of the reference's test files, run only through
+# test_gpu_reference_suite.py (they import `thork`, which that test aliases)
+collect_ignore = ["_reference_suite"]
+
+
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 GPU (runs the CUDA path)")
