@@ -260,8 +260,12 @@ def config_for(name: str, world: int, gather: str = "fused") -> dict:
             "workload": name, "M": size, "N": size, "K": size,
             "dtype_in": kind, "dtype_out": "bf16", "accumulate": "fp32",
             "parallelism": (f"A rows split over {world} GPUs, B replicated, C all-gathered "
-                            + ("inside the GEMM epilogue (P2P stores over NVLink + device flag "
-                               "barrier)" if gather == "fused" else "with NCCL")
+                            + {"fused": "inside the GEMM epilogue (P2P stores over NVLink + device "
+                                        "flag barrier)",
+                               "multimem": "inside the GEMM epilogue (one multimem store per line "
+                                           "through an NVLink multicast buffer + device flag "
+                                           "barrier)",
+                               "nccl": "with NCCL"}[gather]
                             if world > 1 else "1 GPU"),
             "l2_policy": (f"A + B + C = {ws:.0f} MiB > 2x L2 (126 MB): no flush needed"
                           if copies == 1 else
@@ -358,7 +362,7 @@ class GemmWorkload:
         self.i = 0
         self.gather = gather if d.world > 1 else "none"
         rows_out = self.m if d.world > 1 else self.m_loc
-        self.C = rt.empty((rows_out, self.n), np.uint16) if self.gather != "fused" else None
+        self.C = rt.empty((rows_out, self.n), np.uint16) if self.gather in ("none", "nccl") else None
         self.comm = comm
         self.own_comm = False
         self.fg = None
@@ -373,10 +377,11 @@ class GemmWorkload:
                 uid = d.bcast_bytes(uid)
                 self.comm = dist_mod.Communicator(d.rank, d.world, unique_id=uid)
                 self.own_comm = True
-            if self.gather == "fused":
-                self.fg = dist_mod.FusedGather(self.comm, self.m, self.n)
+            if self.gather in ("fused", "multimem"):
+                self.fg = dist_mod.FusedGather(self.comm, self.m, self.n,
+                                               mode="multimem" if self.gather == "multimem" else "p2p")
         # our kernels per step: the GEMM, plus the flag barrier when fused
-        self.launches_per_step = 2 if self.gather == "fused" else 1
+        self.launches_per_step = 2 if self.fg is not None else 1
         self.last = None
 
     flops_total = property(lambda self: 2.0 * self.m * self.n * self.k)
@@ -868,7 +873,7 @@ def also_measurements(args, d, rt, dist_mod, peaks, main=None, sampler=None, ms_
                 ("skinny_m128", 300))
     comm = main.comm if isinstance(main, GemmWorkload) else None
     for name, steps in plan:
-        w = make_workload(name, d, rt, dist_mod, comm=comm)
+        w = make_workload(name, d, rt, dist_mod, gather=args.gather, comm=comm)
         out[name] = _also_entry(w, d, rt, peaks, steps)
         w.close()
         del w
@@ -1150,8 +1155,9 @@ def main():
     ap.add_argument("--workload", default="bf16_gemm_8192")
     ap.add_argument("--impl", default="thork", choices=["thork", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--gather", default="fused", choices=["fused", "nccl"],
-                    help="multi-GPU GEMM: all-gather fused into the epilogue, or NCCL after it")
+    ap.add_argument("--gather", default="fused", choices=["fused", "multimem", "nccl"],
+                    help="multi-GPU GEMM: all-gather fused into the epilogue (P2P stores, or "
+                         "multimem stores through an NVLink multicast buffer), or NCCL after it")
     ap.add_argument("--no-also", dest="also", action="store_false",
                     help="omit the short timings of the other configs")
     args = ap.parse_args()

@@ -248,6 +248,18 @@ THORK_API int thork_gemm_e4m3_allgather(const void *d_a_rows, const void *d_b, v
                                         void *const *d_peer_c, int n_peers, int rows, int N, int K,
                                         int row0, unsigned *d_tile_flags, unsigned epoch,
                                         float scale_a, float scale_b, int variant, void *stream);
+/* Fused GEMM + all-gather through an NVLink multicast buffer: rows
+ * [row0, row0+rows) of C = A_rows . B are written once, with multimem
+ * stores, to d_c_multicast (the multicast view, thork_mc_bind, of a full
+ * M x N bf16 result), which places them in every member GPU's memory.
+ * Pair with thork_peer_barrier as for thork_gemm_bf16_allgather.  bf16:
+ * K, N multiples of 8; e4m3: multiples of 16, C scaled by scale_a*scale_b.
+ * No reference counterpart.                                                */
+THORK_API int thork_gemm_bf16_allgather_mc(const void *d_a_rows, const void *d_b, void *d_c_multicast,
+                                           int rows, int N, int K, int row0, void *stream);
+THORK_API int thork_gemm_e4m3_allgather_mc(const void *d_a_rows, const void *d_b, void *d_c_multicast,
+                                           int rows, int N, int K, int row0, float scale_a,
+                                           float scale_b, void *stream);
 /* Device-side barrier of the fused all-gather: this rank stores `epoch` into
  * slot `rank` of every peer's flag array (d_peer_flags[q], q != rank, each
  * `world` unsigned words in the peer's memory opened with thork_ipc_open)
@@ -307,6 +319,36 @@ THORK_API int thork_skinny_gemm_bf16_noalloc(const void *d_x, const void *d_w, v
  * and resets it when clear != 0.  Allocates nothing.  No reference
  * counterpart.                                                             */
 THORK_API int thork_skinny_gemm_bf16_noalloc_status(unsigned *status, int clear, void *stream);
+
+/* ---- NVLink multicast buffers (no reference counterpart) ---------------
+ * For the fused GEMM + all-gather over NVSwitch multicast ("NVLS"): every
+ * GPU of a group binds memory of its own to one multicast object, and a
+ * `multimem.st` to the multicast view from any GPU lands at the same offset
+ * in every GPU's memory.  One process per GPU:
+ *   1. one rank: thork_mc_create (the object and a POSIX descriptor to hand
+ *      to the others, e.g. over a Unix socket); the others: thork_mc_import
+ *      (the caller closes its received descriptor afterwards);
+ *   2. every rank: thork_mc_add_device; then a host barrier;
+ *   3. every rank: thork_mc_bind -> this GPU's ordinary (unicast) view and
+ *      the multicast view; then a host barrier before any store;
+ *   4. every rank, after a host barrier that no kernel is still storing:
+ *      thork_mc_release (unmaps, unbinds and frees; closes the creator's
+ *      descriptor).
+ * A rank should not exit while its memory is bound: release it first.      */
+/* *supported = 1 when the current device can join multicast objects shared
+ * through POSIX file descriptors.                                          */
+THORK_API int thork_mc_supported(int *supported);
+/* Creates an object for `ndev` GPUs of at least `bytes` (rounded up to the
+ * multicast granularity: *bytes_rounded).  *fd is owned by the object.     */
+THORK_API int thork_mc_create(size_t bytes, int ndev, void **obj, int *fd, size_t *bytes_rounded);
+/* Imports an object from a descriptor; `bytes_rounded` as reported by the
+ * creator.                                                                 */
+THORK_API int thork_mc_import(int fd, size_t bytes_rounded, void **obj);
+/* Adds the current device to the object.                                  */
+THORK_API int thork_mc_add_device(void *obj);
+/* Allocates the current device's memory, binds it and maps both views.    */
+THORK_API int thork_mc_bind(void *obj, void **d_local, void **d_multicast);
+THORK_API int thork_mc_release(void *obj);
 
 /* ---- NCCL (dlopen of libnccl.so.2; no reference counterpart) ---------- */
 /* Writes a 128-byte ncclUniqueId into id128.                              */

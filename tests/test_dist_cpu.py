@@ -165,3 +165,49 @@ def test_replicate_host_rows_copies_one_share_per_rank(monkeypatch, rows, world)
     share = host.nbytes // world if rows % world == 0 else host.nbytes
     assert results == [share] * world
     assert copied == [share] * world  # one copy per rank, of its share
+
+
+def _receive_and_write(name, q):
+    import os
+    from thork_b200 import dist
+    fd, payload = dist.receive_fd(name, timeout=30)
+    os.write(fd, b"from-child:" + payload)
+    os.close(fd)
+    q.put("ok")
+
+
+def test_descriptor_handoff_between_processes():
+    """serve_fd / receive_fd hand a file descriptor (and a payload) to other
+    processes over an abstract Unix socket, as the multicast buffer setup
+    does with the multicast object's descriptor."""
+    import multiprocessing as mp
+    import os
+    import uuid
+    from thork_b200 import dist
+    r, w = os.pipe()
+    name = "thork-test-" + uuid.uuid4().hex[:12]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_receive_and_write, args=(name, q)) for _ in range(2)]
+    for p in procs:
+        p.start()
+    dist.serve_fd(name, w, b"xy", 2, timeout=60)
+    os.close(w)
+    for p in procs:
+        p.join(timeout=60)
+    assert [q.get(timeout=10) for _ in procs] == ["ok", "ok"]
+    data = b""
+    while True:
+        chunk = os.read(r, 100)
+        if not chunk:
+            break
+        data += chunk
+    os.close(r)
+    assert data == b"from-child:xy" * 2
+
+
+def test_receive_fd_times_out_without_server():
+    import uuid
+    from thork_b200 import dist
+    with pytest.raises(TimeoutError):
+        dist.receive_fd("thork-absent-" + uuid.uuid4().hex[:12], timeout=0.2)

@@ -166,3 +166,99 @@ def test_fused_gemm_allgather_over_peer_memory():
         p.join(timeout=300)
     results = dict(q.get(timeout=10) for _ in range(world))
     assert results == {r: "ok" for r in range(world)}, results
+
+
+def _rank_multimem(rank, world, port, q):
+    """The multimem mode: one store per line through an NVLink multicast
+    view.  Every rank runs the same collective steps whatever its checks
+    find (failures are collected, not raised, until the buffer is released),
+    so no rank leaves while its memory is bound to the multicast object."""
+    import datetime
+    import torch.distributed as td
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    td.init_process_group("gloo", rank=rank, world_size=world,
+                          timeout=datetime.timedelta(seconds=60))
+    comm = None
+    problems = []
+    try:
+        import thork_b200 as tk
+        from thork_b200 import dist
+        from oracle import oracle
+        rt = tk.runtime
+        rt.set_device(rank)
+        uid = [None]
+        if rank == 0:
+            import ctypes
+            buf = (ctypes.c_uint8 * 128)()
+            rt.check(rt.lib().thork_nccl_get_unique_id(buf))
+            uid = [bytes(buf)]
+        td.broadcast_object_list(uid, src=0)
+        comm = dist.Communicator(rank, world, unique_id=uid[0])
+        stream = rt.Stream()
+        for m, n, k in ((1024, 768, 512), (1001, 520, 264)):
+            fg = dist.FusedGather(comm, m, n, mode="multimem")
+            try:
+                assert fg.mode == "multimem"
+                b = None
+                for call in range(4):
+                    a, b0 = oracle.gemm_inputs(m, n, k, seed=30 + call)
+                    if b is None:
+                        b = oracle.f32_to_bf16_bits(b0)
+                        B = rt.to_device(b)
+                    a16 = oracle.f32_to_bf16_bits(a)
+                    s, e = dist.row_shard(m, world, rank)
+                    A = rt.to_device(np.ascontiguousarray(a16[s:e]))
+                    got = fg.matmul(A, B, stream).to_host(stream=stream)
+                    err = oracle.max_rel_err(oracle.bf16_bits_to_f32(got), oracle.gemm_bf16_ref(a16, b))
+                    if err > 1e-2:
+                        problems.append(f"{m}x{n}x{k} call {call}: max rel err {err}")
+                    if m % world == 0:
+                        ref = rt.empty((m, n), np.uint16)
+                        dist.sharded_matmul(comm, A, B, ref, m, dtype="bf16", stream=stream)
+                        if not np.array_equal(got, ref.to_host(stream=stream)):
+                            problems.append(f"{m}x{n}x{k} call {call}: differs from NCCL path")
+                if m == 1024:
+                    qa, sa = oracle.quantize_e4m3(a)
+                    qb, sb = oracle.quantize_e4m3(b0)
+                    s, e = dist.row_shard(m, world, rank)
+                    got = fg.matmul(rt.to_device(np.ascontiguousarray(qa[s:e])), rt.to_device(qb),
+                                    stream, dtype="e4m3", scale_a=sa, scale_b=sb).to_host(stream=stream)
+                    err = oracle.max_rel_err(oracle.bf16_bits_to_f32(got),
+                                             oracle.gemm_e4m3_ref(qa, sa, qb, sb))
+                    if err > 1e-2:
+                        problems.append(f"e4m3: max rel err {err}")
+                st = rt.kernel_status(clear=True)
+                if st:
+                    problems.append(f"kernel status {st:#x}")
+            finally:
+                fg.close()
+        q.put((rank, "ok" if not problems else "; ".join(problems)))
+    except Exception as exc:  # noqa: BLE001 - reported to the parent
+        q.put((rank, repr(exc)))
+    finally:
+        if comm is not None:
+            comm.close()
+        td.destroy_process_group()
+
+
+def test_fused_gemm_allgather_through_multicast():
+    import thork_b200 as tk
+    from thork_b200 import dist
+    ndev = tk.runtime.device_count()
+    if ndev < 2:
+        pytest.skip("needs 2 GPUs")
+    tk.runtime.set_device(0)
+    if not dist.multicast_supported():
+        pytest.skip("NVLink multicast not supported here")
+    world = min(ndev, 8)
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_multimem, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    results = dict(q.get(timeout=10) for _ in range(world))
+    assert results == {r: "ok" for r in range(world)}, results

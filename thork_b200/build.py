@@ -21,7 +21,7 @@ LIB_DIR = os.path.join(PKG_DIR, "lib")
 OBJ_DIR = os.path.join(PKG_DIR, "_build")
 LIB_PATH = os.path.join(LIB_DIR, "libthork_rt.so")
 
-SOURCES = ["thork_rt.cu", "kernels.cu", "staging.cu"]
+SOURCES = ["thork_rt.cu", "kernels.cu", "staging.cu", "multicast.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

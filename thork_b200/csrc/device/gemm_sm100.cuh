@@ -85,12 +85,14 @@ struct Params {
   u32 epoch;        // this call's number: a unit is done once its count is 4 * epoch
 };
 
-// Modes of the fused all-gather inside gemm_kernel.
-enum : int { AG_NONE = 0, AG_STAGED = 1, AG_PUSH = 2 };
+// Modes of the fused all-gather inside gemm_kernel: staged peer stores, push
+// warps, or one multicast (NVLS) store per line through `out`, the
+// multicast view of the gathered C.
+enum : int { AG_NONE = 0, AG_STAGED = 1, AG_PUSH = 2, AG_MULTIMEM = 3 };
 
 template <class Cfg, int AG>
 constexpr int gemm_smem_bytes() {
-  return AG == AG_STAGED ? Cfg::SMEM_BYTES_STAGED : Cfg::SMEM_BYTES;
+  return (AG == AG_STAGED || AG == AG_MULTIMEM) ? Cfg::SMEM_BYTES_STAGED : Cfg::SMEM_BYTES;
 }
 template <class Cfg, int AG>
 constexpr int gemm_threads() {
@@ -187,7 +189,9 @@ __device__ __forceinline__ void bf16_store_tile(const Params &p, u32 t_row, int 
 // directions are bank-conflict free), then back out with lanes covering
 // consecutive 16-byte chunks of a row: every warp store writes whole
 // 128-byte lines, to this GPU's C and to each peer's C at the same offset.
-template <class Cfg>
+// MC: `p.out` is a multicast view; each line is stored once with
+// multimem.st and the NVSwitch delivers it to every GPU of the group.
+template <class Cfg, bool MC = false>
 __device__ __forceinline__ void bf16_store_tile_peers(const Params &p, u32 t_row, int row0,
                                                       int col0, unsigned char *stg, int lane) {
   constexpr int EC = Cfg::EPI_COLS;
@@ -224,11 +228,15 @@ __device__ __forceinline__ void bf16_store_tile_peers(const Params &p, u32 t_row
       const int row = row0 + r, col = col0 + c0 + chunk * 8;
       if (row < p.out_rows && col < p.out_cols) {
         const long long off = static_cast<long long>(row) * p.ldo + col;
-        st_global_v4(out + off, v.x, v.y, v.z, v.w);
+        if constexpr (MC) {
+          multimem_st_v4(out + off, v.x, v.y, v.z, v.w);
+        } else {
+          st_global_v4(out + off, v.x, v.y, v.z, v.w);
 #pragma unroll
-        for (int g = 0; g < 7; ++g)  // constant indices keep p.peer in parameter space
-          if (g < p.npeer)
-            st_global_v4(static_cast<unsigned short *>(p.peer[g]) + off, v.x, v.y, v.z, v.w);
+          for (int g = 0; g < 7; ++g)  // constant indices keep p.peer in parameter space
+            if (g < p.npeer)
+              st_global_v4(static_cast<unsigned short *>(p.peer[g]) + off, v.x, v.y, v.z, v.w);
+        }
       }
     }
     __syncwarp();
@@ -477,9 +485,10 @@ __global__ void __launch_bounds__(gemm_threads<Cfg, AG>(), 1)
       tc_fence_after();
       const int row_mma = tm * Cfg::BM + q * 32 + lane;  // MMA-space row owned by this thread
       const u32 t_row = tmem_base + ((u32)(q * 32) << 16) + acc * Cfg::BN;
-      if constexpr (AG == AG_STAGED)
-        bf16_store_tile_peers<Cfg>(p, t_row, tm * Cfg::BM + q * 32, tn * Cfg::BN,
-                                   smem + Cfg::EPI_OFF + q * Cfg::EPI_WARP_BYTES, lane);
+      if constexpr (AG == AG_STAGED || AG == AG_MULTIMEM)
+        bf16_store_tile_peers<Cfg, AG == AG_MULTIMEM>(p, t_row, tm * Cfg::BM + q * 32, tn * Cfg::BN,
+                                                      smem + Cfg::EPI_OFF + q * Cfg::EPI_WARP_BYTES,
+                                                      lane);
       else
         bf16_store_tile<Cfg>(p, t_row, row_mma, tn * Cfg::BN);
       tc_fence_before();
@@ -503,9 +512,10 @@ __global__ void __launch_bounds__(gemm_threads<Cfg, AG>(), 1)
         }
       }
     }
-    // staged peer stores are ordered before anything a later kernel signals
-    // to the peers (the fused all-gather's flag barrier)
-    if constexpr (AG == AG_STAGED) __threadfence_system();
+    // staged peer stores (or multicast stores) are ordered before anything a
+    // later kernel signals to the peers (the fused all-gather's flag barrier)
+    if constexpr (AG == AG_MULTIMEM) fence_proxy_alias();
+    if constexpr (AG == AG_STAGED || AG == AG_MULTIMEM) __threadfence_system();
   }
 
   tc_fence_before();

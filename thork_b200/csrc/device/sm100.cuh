@@ -361,6 +361,18 @@ __device__ __forceinline__ u32 pack_bf16x2(float lo, float hi) {
   return r;
 }
 
+// 16-byte store to a multicast (NVLS) address: the NVSwitch writes it to the
+// same offset in every member GPU's memory, this one included.
+__device__ __forceinline__ void multimem_st_v4(void *p, u32 a, u32 b, u32 c, u32 d) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a),
+               "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
+// Orders this thread's accesses through a multicast view before later ones
+// through an ordinary view of the same memory (and the reverse).
+__device__ __forceinline__ void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
+
 __device__ __forceinline__ void st_global_v4(void *p, u32 a, u32 b, u32 c, u32 d) {
   asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d)
                : "memory");

@@ -252,7 +252,8 @@ using CfgSkinny256 = Config<KIND_BF16, 256, 4, true, false, true>;
 enum KernelId {
   K_GEMM_BF16 = 0, K_GEMM_E4M3, K_SKINNY64, K_SKINNY128, K_SKINNY256,
   K_GEMM2_BF16, K_GEMM2_E4M3, K_SKSK16, K_SKSK32, K_GEMM_BF16_SK, K_GEMM_E4M3_SK,
-  K_AG_BF16, K_AGP_BF16, K_AG_E4M3, K_AGP_E4M3  // fused all-gather: staged, push warps
+  K_AG_BF16, K_AGP_BF16, K_AG_E4M3, K_AGP_E4M3,  // fused all-gather: staged, push warps
+  K_AGM_BF16, K_AGM_E4M3                         // fused all-gather through a multicast view
 };
 
 template <class Cfg, int AG = AG_NONE>
@@ -437,6 +438,45 @@ extern "C" int thork_gemm_e4m3_allgather(const void *d_a_rows, const void *d_b, 
 }
 
 namespace {
+// Fused GEMM + all-gather through a multicast view: this rank's rows are
+// stored once, with multimem.st, at their offset of the gathered C.
+template <class Cfg>
+int gemm_allgather_mc(int kid, int dt, int elem, const void *d_a_rows, const void *d_b, void *d_c_mc,
+                      int rows, int N, int K, int row0, float alpha, void *stream, const char *what) {
+  int rc;
+  if ((rc = check_dims(rows, N, K, 16 / elem, what))) return rc;
+  if ((rc = check_ptrs(d_a_rows, d_b, d_c_mc, what))) return rc;
+  if (row0 < 0) return thork_set_error(THORK_ERR_INVALID, "%s: row0 < 0", what);
+  if (reinterpret_cast<uintptr_t>(d_c_mc) & 15u)
+    return thork_set_error(THORK_ERR_INVALID, "%s: multicast view not 16-byte aligned", what);
+  alignas(64) TensorMap ta, tb;
+  if ((rc = thork_encode_tmap_2d(&ta, dt, d_a_rows, rows, K, (uint64_t)K * elem, Cfg::BM, Cfg::BK,
+                                 128)))
+    return rc;
+  if ((rc = thork_encode_tmap_2d(&tb, dt, d_b, K, N, (uint64_t)N * elem, Cfg::BK, Cfg::CHUNK, 128)))
+    return rc;
+  unsigned *status;
+  if ((rc = thork_status_word(&status))) return rc;
+  const size_t off = static_cast<size_t>(row0) * N * 2;
+  Params prm{static_cast<char *>(d_c_mc) + off, rows, N, K, N, rows, N, alpha, status};
+  return run_gemm<Cfg, AG_MULTIMEM>(kid, ta, tb, prm, static_cast<cudaStream_t>(stream), what);
+}
+}  // namespace
+
+extern "C" int thork_gemm_bf16_allgather_mc(const void *d_a_rows, const void *d_b, void *d_c_mc,
+                                           int rows, int N, int K, int row0, void *stream) {
+  return gemm_allgather_mc<CfgBf16>(K_AGM_BF16, THORK_DT_BF16, 2, d_a_rows, d_b, d_c_mc, rows, N, K,
+                                    row0, 1.0f, stream, "gemm_bf16_allgather_mc");
+}
+
+extern "C" int thork_gemm_e4m3_allgather_mc(const void *d_a_rows, const void *d_b, void *d_c_mc,
+                                           int rows, int N, int K, int row0, float scale_a,
+                                           float scale_b, void *stream) {
+  return gemm_allgather_mc<CfgE4m3>(K_AGM_E4M3, THORK_DT_E4M3, 1, d_a_rows, d_b, d_c_mc, rows, N, K,
+                                    row0, scale_a * scale_b, stream, "gemm_e4m3_allgather_mc");
+}
+
+namespace {
 // Flag barrier between the ranks of a fused all-gather.  Rank r stores
 // `epoch` into flags[r] of every peer (release at system scope, after a
 // system fence that orders this GPU's earlier peer stores), then waits, at
@@ -470,6 +510,9 @@ __global__ void peer_barrier_kernel(const PeerFlagPtrs peers, unsigned *flags, i
       __nanosleep(64);
     }
   }
+  // what the peers stored through a multicast view is read through this
+  // GPU's ordinary view after the barrier
+  thork::dev::fence_proxy_alias();
   __syncthreads();
 }
 }  // namespace

@@ -23,6 +23,9 @@ hard-codes device 0, ``src/thork/runtime.py:85-105``).
 """
 
 import ctypes
+import hashlib
+import os
+import struct
 from typing import Callable, Optional, Tuple
 
 import numpy as np
@@ -120,6 +123,103 @@ class Communicator:
             self.handle = None
 
 
+def serve_fd(name: str, fd: int, payload: bytes, nclients: int, timeout: float = 60.0) -> None:
+    """Hand ``fd`` (and ``payload``) to ``nclients`` processes that call
+    ``receive_fd(name)``: an abstract-namespace Unix socket, SCM_RIGHTS
+    messages.  Returns once every client has been served; raises
+    ``TimeoutError`` when one does not connect in time."""
+    import socket
+    srv = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+    try:
+        srv.bind("\0" + name)
+        srv.listen(max(nclients, 1))
+        srv.settimeout(timeout)
+        for _ in range(nclients):
+            try:
+                conn, _ = srv.accept()
+            except socket.timeout as e:
+                raise TimeoutError(f"serve_fd({name}): a client did not connect") from e
+            with conn:
+                socket.send_fds(conn, [payload], [fd])
+    finally:
+        srv.close()
+
+
+def receive_fd(name: str, timeout: float = 60.0):
+    """The client side of ``serve_fd``: returns (fd, payload); the caller
+    owns and closes the received descriptor."""
+    import socket
+    import time
+    t0 = time.monotonic()
+    while True:
+        cli = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+        try:
+            cli.connect("\0" + name)
+            cli.settimeout(timeout)
+            payload, fds, _, _ = socket.recv_fds(cli, 4096, 1)
+            if not fds:
+                raise RuntimeError(f"receive_fd({name}): no descriptor received")
+            return fds[0], payload
+        except (ConnectionRefusedError, FileNotFoundError):
+            if time.monotonic() - t0 > timeout:
+                raise TimeoutError(f"receive_fd({name}): nobody serves it") from None
+            time.sleep(0.01)
+        finally:
+            cli.close()
+
+
+class _Multicast:
+    """This rank's part of an NVLink multicast buffer (``thork_mc_*``): one
+    object for the group, this GPU's memory bound to it, an ordinary view
+    (``local``) and a multicast view (``multi``) where one store reaches
+    every GPU.  ``barrier`` is a host barrier over the group."""
+
+    def __init__(self, rank: int, world: int, nbytes: int, name: str, barrier: Callable[[], None]):
+        L = rt.lib()
+        self.obj = None
+        if rank == 0:
+            obj, fd, size = ctypes.c_void_p(), ctypes.c_int(), ctypes.c_size_t()
+            rt.check(L.thork_mc_create(nbytes, world, ctypes.byref(obj), ctypes.byref(fd),
+                                       ctypes.byref(size)), "multicast create")
+            self.obj, self.bytes = obj.value, size.value
+            try:
+                serve_fd(name, fd.value, struct.pack("<Q", self.bytes), world - 1)
+            except Exception:
+                L.thork_mc_release(self.obj)
+                self.obj = None
+                raise
+        else:
+            fd, payload = receive_fd(name)
+            try:
+                self.bytes = struct.unpack("<Q", payload[:8])[0]
+                obj = ctypes.c_void_p()
+                rt.check(L.thork_mc_import(fd, self.bytes, ctypes.byref(obj)), "multicast import")
+                self.obj = obj.value
+            finally:
+                os.close(fd)
+        rt.check(L.thork_mc_add_device(self.obj), "multicast add device")
+        barrier()  # every device is added before any memory is bound
+        local, multi = ctypes.c_void_p(), ctypes.c_void_p()
+        rt.check(L.thork_mc_bind(self.obj, ctypes.byref(local), ctypes.byref(multi)),
+                 "multicast bind")
+        self.local, self.multi = local.value, multi.value
+        rt.check(L.thork_memset(self.local, 0, self.bytes, None), "multicast buffer clear")
+        rt.check(L.thork_device_synchronize(), "synchronize")
+        barrier()  # every GPU's memory is bound and clear before any store
+
+    def release(self) -> None:
+        if self.obj:
+            rt.check(rt.lib().thork_mc_release(self.obj), "multicast release")
+            self.obj = None
+
+
+def multicast_supported() -> bool:
+    """Whether the current GPU can join NVLink multicast buffers."""
+    v = ctypes.c_int(0)
+    rt.check(rt.lib().thork_mc_supported(ctypes.byref(v)), "multicast supported")
+    return bool(v.value)
+
+
 class _View:
     """A borrowed device pointer in the shape ``DeviceArray`` expects of its
     buffer (no ownership)."""
@@ -144,22 +244,44 @@ class FusedGather:
     (``thork_peer_barrier``) then orders every peer's stores before whatever
     this rank queues next.  No NCCL call is on the data path.
 
+    ``mode="multimem"``: the result slots live in an NVLink multicast buffer
+    instead (``thork_mc_*``: every GPU's memory bound to one multicast
+    object); the epilogue stores each line of this rank's rows once through
+    the multicast view and the NVSwitch delivers it to every GPU, so the
+    GPU's outgoing NVLink traffic and store count do not grow with the
+    number of peers.  Only the flag page is exchanged through CUDA IPC.
+    ``mode="auto"`` takes multimem when every GPU supports it.
+
     Results rotate through the slots: consume a call's result (stream-ordered
     on this rank) before making the next call.  Requires one GPU per rank
-    and at most 8 ranks.
+    and at most 8 ranks.  ``close()`` is collective; with multimem, call it
+    (every rank) before the process exits.
     """
 
     SLOTS = 2
 
-    def __init__(self, comm: Communicator, m_total: int, n: int):
+    def __init__(self, comm: Communicator, m_total: int, n: int, mode: str = "p2p"):
         L = rt.lib()
         self.comm = comm
         self.rank, self.world = comm.rank, comm.world
         if not (1 <= self.world <= 8):
             raise ValueError(f"fused all-gather supports 1..8 ranks, got {self.world}")
+        if mode not in ("p2p", "multimem", "auto"):
+            raise ValueError(f"unknown fused all-gather mode {mode!r}")
         self.m_total, self.n = int(m_total), int(n)
         self.slot_bytes = ((self.m_total * self.n * 2 + 255) // 256) * 256
-        self.flag_off = self.SLOTS * self.slot_bytes
+        self.mc = None
+        if mode == "auto":
+            # every rank must take the same decision: agree through NCCL
+            flag = rt.DeviceArray((1,), np.float32)
+            rt.copy_htod(flag.ptr, np.array([1.0 if multicast_supported() else 0.0], np.float32))
+            comm.allreduce_sum(flag.ptr, 1, DT_F32)
+            rt.check(L.thork_device_synchronize(), "synchronize")
+            mode = "multimem" if flag.to_host()[0] == self.world and self.world > 1 else "p2p"
+        self.mode = mode
+        # p2p: the slots and the flag page in one IPC-shared allocation;
+        # multimem: only the flag page is shared through IPC
+        self.flag_off = self.SLOTS * self.slot_bytes if mode == "p2p" else 0
         self.total_bytes = self.flag_off + 256
         dev = rt.get_device()
         base = ctypes.c_void_p()
@@ -211,8 +333,28 @@ class FusedGather:
         # any peer store can arrive
         comm.allgather(send.ptr, recv.ptr, rec, 0)
         rt.check(L.thork_device_synchronize(), "synchronize")
+        if mode == "multimem":
+            name = "thork-mc-" + hashlib.sha1(allrec[0, :64].tobytes()).hexdigest()[:24]
+            try:
+                self.mc = _Multicast(self.rank, self.world, self.SLOTS * self.slot_bytes, name,
+                                     self._host_barrier)
+            except Exception:
+                self._close_peers()
+                self._free_own()
+                raise
+
+    def _host_barrier(self) -> None:
+        """Every rank has reached this point (an NCCL all-reduce, waited on)."""
+        if getattr(self, "_bar", None) is None:
+            self._bar = rt.DeviceArray((1,), np.float32)
+        self.comm.allreduce_sum(self._bar.ptr, 1, DT_F32)
+        rt.check(rt.lib().thork_device_synchronize(), "synchronize")
 
     def slot_ptr(self, slot: int, rank: Optional[int] = None) -> int:
+        if self.mc is not None:
+            if rank is not None and rank != self.rank:
+                raise ValueError("multimem mode maps no peer result buffers")
+            return self.mc.local + (slot % self.SLOTS) * self.slot_bytes
         b = self.base if rank is None else self.peer_base[rank]
         return b + (slot % self.SLOTS) * self.slot_bytes
 
@@ -244,9 +386,22 @@ class FusedGather:
                              f"shard {stop - start} x {k}, N {self.n}")
         slot = self.calls % self.SLOTS
         self.calls += 1  # also the epoch of the tile flags
-        peers = (ctypes.c_void_p * 7)(*[self.slot_ptr(slot, q) for q in self.peers])
         sh = stream.handle if stream else None
         L = rt.lib()
+        if self.mc is not None:
+            dst = self.mc.multi + slot * self.slot_bytes
+            if dtype == "bf16":
+                rc = L.thork_gemm_bf16_allgather_mc(a_local.ptr, b.ptr, dst, stop - start, self.n, k,
+                                                    start, sh)
+            else:
+                rc = L.thork_gemm_e4m3_allgather_mc(a_local.ptr, b.ptr, dst, stop - start, self.n, k,
+                                                    start, float(scale_a), float(scale_b), sh)
+            rt.check(rc, "fused gemm + multicast all-gather")
+            if gemm_done is not None:
+                gemm_done.record(stream)
+            self.barrier(stream)
+            return self.result(slot)
+        peers = (ctypes.c_void_p * 7)(*[self.slot_ptr(slot, q) for q in self.peers])
         args = (a_local.ptr, b.ptr, self.slot_ptr(slot), peers, len(self.peers), stop - start,
                 self.n, k, start, self.tile_flags.ptr, self.calls & 0xFFFFFFFF)
         if dtype == "bf16":
@@ -278,6 +433,10 @@ class FusedGather:
         rt.check(rt.lib().thork_device_synchronize(), "synchronize")
         self.barrier(None)
         rt.check(rt.lib().thork_device_synchronize(), "synchronize")
+        if self.mc is not None:
+            self._host_barrier()  # no rank stores through the multicast view any more
+            self.mc.release()
+            self.mc = None
         self._close_peers()
         self._free_own()
 

@@ -102,6 +102,15 @@ _SIGNATURES = {
     "thork_ipc_handle": [_vp, _vp],
     "thork_ipc_open": [_vp, _pvp],
     "thork_ipc_close": [_vp],
+    "thork_gemm_bf16_allgather_mc": [_vp, _vp, _vp, _i, _i, _i, _i, _vp],
+    "thork_gemm_e4m3_allgather_mc": [_vp, _vp, _vp, _i, _i, _i, _i, ctypes.c_float,
+                                     ctypes.c_float, _vp],
+    "thork_mc_supported": [ctypes.POINTER(_i)],
+    "thork_mc_create": [_sz, _i, _pvp, ctypes.POINTER(_i), ctypes.POINTER(_sz)],
+    "thork_mc_import": [_i, _sz, _pvp],
+    "thork_mc_add_device": [_vp],
+    "thork_mc_bind": [_vp, _pvp, _pvp],
+    "thork_mc_release": [_vp],
     "thork_nccl_get_unique_id": [_vp],
     "thork_nccl_comm_init_rank": [_pvp, _i, _vp, _i],
     "thork_nccl_comm_destroy": [_vp],
