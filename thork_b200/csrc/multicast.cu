@@ -60,7 +60,9 @@ template <class F>
 bool entry(const char *name, F *out) {
   void *p = nullptr;
   cudaDriverEntryPointQueryResult q;
-  cudaError_t e = cudaGetDriverEntryPointByVersion(name, &p, 12000, cudaEnableDefault, &q);
+  // the multicast entry points first appeared in CUDA 12.1: ask for the
+  // versions of the toolkit this library was built with
+  cudaError_t e = cudaGetDriverEntryPointByVersion(name, &p, CUDA_VERSION, cudaEnableDefault, &q);
   if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !p) return false;
   *out = reinterpret_cast<F>(p);
   return true;

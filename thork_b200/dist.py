@@ -172,45 +172,72 @@ class _Multicast:
     """This rank's part of an NVLink multicast buffer (``thork_mc_*``): one
     object for the group, this GPU's memory bound to it, an ordinary view
     (``local``) and a multicast view (``multi``) where one store reaches
-    every GPU.  ``barrier`` is a host barrier over the group."""
+    every GPU.
 
-    def __init__(self, rank: int, world: int, nbytes: int, name: str, barrier: Callable[[], None]):
-        L = rt.lib()
+    Every set-up step ends with ``agree(ok)`` (True only if every rank's
+    step succeeded), so all ranks take the same path: when any rank fails,
+    every rank releases what it holds and raises, and no rank is left
+    waiting in a collective while its memory is bound."""
+
+    def __init__(self, rank: int, world: int, nbytes: int, name: str,
+                 agree: Callable[[bool], bool]):
         self.obj = None
-        if rank == 0:
-            obj, fd, size = ctypes.c_void_p(), ctypes.c_int(), ctypes.c_size_t()
-            rt.check(L.thork_mc_create(nbytes, world, ctypes.byref(obj), ctypes.byref(fd),
-                                       ctypes.byref(size)), "multicast create")
-            self.obj, self.bytes = obj.value, size.value
-            try:
+        self.local = self.multi = 0
+        L = rt.lib()
+        err = None
+        try:
+            if rank == 0:
+                obj, fd, size = ctypes.c_void_p(), ctypes.c_int(), ctypes.c_size_t()
+                rt.check(L.thork_mc_create(nbytes, world, ctypes.byref(obj), ctypes.byref(fd),
+                                           ctypes.byref(size)), "multicast create")
+                self.obj, self.bytes = obj.value, size.value
                 serve_fd(name, fd.value, struct.pack("<Q", self.bytes), world - 1)
-            except Exception:
-                L.thork_mc_release(self.obj)
-                self.obj = None
-                raise
-        else:
-            fd, payload = receive_fd(name)
-            try:
-                self.bytes = struct.unpack("<Q", payload[:8])[0]
-                obj = ctypes.c_void_p()
-                rt.check(L.thork_mc_import(fd, self.bytes, ctypes.byref(obj)), "multicast import")
-                self.obj = obj.value
-            finally:
-                os.close(fd)
-        rt.check(L.thork_mc_add_device(self.obj), "multicast add device")
-        barrier()  # every device is added before any memory is bound
-        local, multi = ctypes.c_void_p(), ctypes.c_void_p()
-        rt.check(L.thork_mc_bind(self.obj, ctypes.byref(local), ctypes.byref(multi)),
-                 "multicast bind")
-        self.local, self.multi = local.value, multi.value
-        rt.check(L.thork_memset(self.local, 0, self.bytes, None), "multicast buffer clear")
-        rt.check(L.thork_device_synchronize(), "synchronize")
-        barrier()  # every GPU's memory is bound and clear before any store
+            else:
+                fd, payload = receive_fd(name)
+                try:
+                    self.bytes = struct.unpack("<Q", payload[:8])[0]
+                    obj = ctypes.c_void_p()
+                    rt.check(L.thork_mc_import(fd, self.bytes, ctypes.byref(obj)),
+                             "multicast import")
+                    self.obj = obj.value
+                finally:
+                    os.close(fd)
+        except Exception as e:  # noqa: BLE001 - decided together below
+            err = e
+        self._step(agree, err, "share the multicast object")
+        self._step(agree, self._try(lambda: rt.check(L.thork_mc_add_device(self.obj),
+                                                     "multicast add device")),
+                   "add every device")
+
+        def bind():
+            local, multi = ctypes.c_void_p(), ctypes.c_void_p()
+            rt.check(L.thork_mc_bind(self.obj, ctypes.byref(local), ctypes.byref(multi)),
+                     "multicast bind")
+            self.local, self.multi = local.value, multi.value
+            rt.check(L.thork_memset(self.local, 0, self.bytes, None), "multicast buffer clear")
+            rt.check(L.thork_device_synchronize(), "synchronize")
+        # every GPU's memory is bound and clear before any store
+        self._step(agree, self._try(bind), "bind every GPU's memory")
+
+    @staticmethod
+    def _try(fn):
+        try:
+            fn()
+            return None
+        except Exception as e:  # noqa: BLE001 - decided together by the caller
+            return e
+
+    def _step(self, agree, err, what: str) -> None:
+        if agree(err is None):
+            return
+        self.release()
+        raise RuntimeError(f"multicast buffer: could not {what} on every rank"
+                           + (f" (this rank: {err})" if err is not None else ""))
 
     def release(self) -> None:
         if self.obj:
-            rt.check(rt.lib().thork_mc_release(self.obj), "multicast release")
-            self.obj = None
+            obj, self.obj = self.obj, None
+            rt.check(rt.lib().thork_mc_release(obj), "multicast release")
 
 
 def multicast_supported() -> bool:
@@ -337,18 +364,24 @@ class FusedGather:
             name = "thork-mc-" + hashlib.sha1(allrec[0, :64].tobytes()).hexdigest()[:24]
             try:
                 self.mc = _Multicast(self.rank, self.world, self.SLOTS * self.slot_bytes, name,
-                                     self._host_barrier)
+                                     self._agree)
             except Exception:
                 self._close_peers()
                 self._free_own()
                 raise
 
-    def _host_barrier(self) -> None:
-        """Every rank has reached this point (an NCCL all-reduce, waited on)."""
+    def _agree(self, ok: bool) -> bool:
+        """Collective: True when every rank passes ok=True (an NCCL sum,
+        waited on); also a host barrier."""
         if getattr(self, "_bar", None) is None:
             self._bar = rt.DeviceArray((1,), np.float32)
+        rt.copy_htod(self._bar.ptr, np.array([1.0 if ok else 0.0], np.float32))
         self.comm.allreduce_sum(self._bar.ptr, 1, DT_F32)
         rt.check(rt.lib().thork_device_synchronize(), "synchronize")
+        return float(self._bar.to_host()[0]) == float(self.world)
+
+    def _host_barrier(self) -> None:
+        self._agree(True)
 
     def slot_ptr(self, slot: int, rank: Optional[int] = None) -> int:
         if self.mc is not None:
