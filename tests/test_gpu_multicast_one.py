@@ -1,5 +1,6 @@
 """The NVLink multicast buffer C-ABI (thork_mc_*) and the multimem fused
-GEMM epilogue on one GPU: a multicast object whose only member is this GPU.
+GEMM epilogue on one GPU: a multicast object whose only member is this GPU
+(skipped where the driver refuses a one-GPU group, as driver 580 does).
 A store through the multicast view lands in this GPU's memory, so the
 result read through the ordinary view must equal the plain GEMM's bit for
 bit (same 128 x 256 tiles).  Multi-GPU groups are covered by
@@ -43,7 +44,10 @@ def test_multimem_epilogue_on_a_one_gpu_group(dtype):
     else:
         rt.check(L.thork_gemm_e4m3(A.ptr, B.ptr, want.ptr, m, n, k, sa, sb, 1, None))
     obj, fd, size = ctypes.c_void_p(), ctypes.c_int(), ctypes.c_size_t()
-    rt.check(L.thork_mc_create(m * n * 2, 1, ctypes.byref(obj), ctypes.byref(fd), ctypes.byref(size)))
+    rc = L.thork_mc_create(m * n * 2, 1, ctypes.byref(obj), ctypes.byref(fd), ctypes.byref(size))
+    if rc != 0 and "CUDA_ERROR_INVALID_VALUE" in rt.last_error():
+        pytest.skip("this driver refuses a multicast group of one GPU")
+    rt.check(rc)
     try:
         assert size.value >= m * n * 2 and fd.value >= 0
         rt.check(L.thork_mc_add_device(obj))
