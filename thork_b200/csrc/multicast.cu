@@ -145,11 +145,15 @@ CUmulticastObjectProp mc_prop(int ndev, size_t bytes) {
   return p;
 }
 
+// Memory bound to a multicast object must be shareable with the object's
+// handle type (measured: cuMulticastBindMem refuses memory created without
+// it with CUDA_ERROR_INVALID_VALUE).
 CUmemAllocationProp phys_prop(CUdevice dev) {
   CUmemAllocationProp p = {};
   p.type = CU_MEM_ALLOCATION_TYPE_PINNED;
   p.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
   p.location.id = static_cast<int>(dev);
+  p.requestedHandleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
   return p;
 }
 
