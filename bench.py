@@ -250,7 +250,9 @@ def skinny_copies(n_loc: int) -> int:
     return max(3, int(math.ceil(3 * L2_BYTES / (SKINNY_K * n_loc * 2))))
 
 
-def config_for(name: str, world: int, gather: str = "fused") -> dict:
+def config_for(name: str, world: int, gather: str = "auto") -> dict:
+    if gather == "auto":  # as FusedGather(mode="auto") resolves it on multicast-capable GPUs
+        gather = "multimem" if world >= 3 else "fused"
     if name in GEMMS:
         size, kind = GEMMS[name]
         copies = gemm_copies(size, kind)
@@ -377,9 +379,11 @@ class GemmWorkload:
                 uid = d.bcast_bytes(uid)
                 self.comm = dist_mod.Communicator(d.rank, d.world, unique_id=uid)
                 self.own_comm = True
-            if self.gather in ("fused", "multimem"):
-                self.fg = dist_mod.FusedGather(self.comm, self.m, self.n,
-                                               mode="multimem" if self.gather == "multimem" else "p2p")
+            if self.gather in ("auto", "fused", "multimem"):
+                self.fg = dist_mod.FusedGather(
+                    self.comm, self.m, self.n,
+                    mode={"auto": "auto", "fused": "p2p", "multimem": "multimem"}[self.gather])
+                self.gather = "multimem" if self.fg.mode == "multimem" else "fused"
         # our kernels per step: the GEMM, plus the flag barrier when fused
         self.launches_per_step = 2 if self.fg is not None else 1
         self.last = None
@@ -661,7 +665,7 @@ class AddWorkload:
         pass
 
 
-def make_workload(name, d, rt, dist_mod, gather="fused", comm=None):
+def make_workload(name, d, rt, dist_mod, gather="auto", comm=None):
     if name in GEMMS:
         size, kind = GEMMS[name]
         return GemmWorkload(size, kind, d, rt, dist_mod, gather, comm=comm)
@@ -735,7 +739,8 @@ def run_thork(args, d: Dist):
     sampler = ClockSampler(d.local_rank)
     sampler.start()
     w = make_workload(args.workload, d, rt, dist_mod, args.gather)
-    cfg = config_for(args.workload, d.world, args.gather)
+    cfg = config_for(args.workload, d.world,
+                     w.gather if isinstance(w, GemmWorkload) and d.world > 1 else args.gather)
     unit, bound = unit_of(w)
 
     total_ms, kernel_ms, tw0, tw1 = time_steps(w, rt, args.steps, args.warmup, d)
@@ -1155,9 +1160,10 @@ def main():
     ap.add_argument("--workload", default="bf16_gemm_8192")
     ap.add_argument("--impl", default="thork", choices=["thork", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--gather", default="fused", choices=["fused", "multimem", "nccl"],
+    ap.add_argument("--gather", default="auto", choices=["auto", "fused", "multimem", "nccl"],
                     help="multi-GPU GEMM: all-gather fused into the epilogue (P2P stores, or "
-                         "multimem stores through an NVLink multicast buffer), or NCCL after it")
+                         "multimem stores through an NVLink multicast buffer; auto: multimem "
+                         "from 3 GPUs where supported), or NCCL after it")
     ap.add_argument("--no-also", dest="also", action="store_false",
                     help="omit the short timings of the other configs")
     args = ap.parse_args()

@@ -86,3 +86,10 @@ def test_checked_combines_single_rank(bench):
     assert bad["pass"] is False
     neq = bench.checked(One(), {"max_rel_err": 0.0, "tolerance": 1e-2, "bitequal_vs_nccl": False})
     assert neq["pass"] is False
+
+
+def test_auto_gather_config_names_the_resolved_mode(bench):
+    assert "multimem" in bench.config_for("bf16_gemm_8192", 8, "auto")["parallelism"]
+    assert "P2P" in bench.config_for("bf16_gemm_8192", 2, "auto")["parallelism"]
+    assert bench.config_for("bf16_gemm_8192", 1, "auto")["parallelism"] == "1 GPU"
+    assert bench.config_for("bf16_gemm_8192", 4, "auto") == bench.config_for("bf16_gemm_8192", 4, "multimem")

@@ -277,7 +277,8 @@ class FusedGather:
     the multicast view and the NVSwitch delivers it to every GPU, so the
     GPU's outgoing NVLink traffic and store count do not grow with the
     number of peers.  Only the flag page is exchanged through CUDA IPC.
-    ``mode="auto"`` takes multimem when every GPU supports it.
+    ``mode="auto"`` takes multimem for three or more ranks when every GPU
+    supports it, else p2p.
 
     Results rotate through the slots: consume a call's result (stream-ordered
     on this rank) before making the next call.  Requires one GPU per rank
@@ -304,7 +305,9 @@ class FusedGather:
             rt.copy_htod(flag.ptr, np.array([1.0 if multicast_supported() else 0.0], np.float32))
             comm.allreduce_sum(flag.ptr, 1, DT_F32)
             rt.check(L.thork_device_synchronize(), "synchronize")
-            mode = "multimem" if flag.to_host()[0] == self.world and self.world > 1 else "p2p"
+            # at two ranks both ways measured the same; from three on, one
+            # multicast store per line beats a store per peer
+            mode = "multimem" if flag.to_host()[0] == self.world and self.world >= 3 else "p2p"
         self.mode = mode
         # p2p: the slots and the flag page in one IPC-shared allocation;
         # multimem: only the flag page is shared through IPC
