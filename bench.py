@@ -411,6 +411,16 @@ class GemmWorkload:
                                  gemm_done=ev1)
         self.last = self.C
 
+    def device_barrier(self, stream):
+        """Line the GPUs up on the device before a timed region: the fused
+        gather's flag barrier, or an NCCL all-reduce (stream-ordered)."""
+        if self.fg is not None:
+            self.fg.barrier(stream)
+        elif self.comm is not None:
+            if getattr(self, "_bar", None) is None:
+                self._bar = self.rt.empty((1,), np.float32)
+            self.comm.allreduce_sum(self._bar.ptr, 1, self.dist.DT_F32, stream)
+
     def local_step(self, stream, ev0=None, ev1=None):
         """This rank's GEMM alone, without the all-gather (scaling reference)."""
         if getattr(self, "C_loc", None) is None:
@@ -698,6 +708,12 @@ def time_steps(w, rt, steps, warmup, d, per_launch_events=True, sample_every=10)
     rt.synchronize()
     d.barrier()
     t_wall0 = time.perf_counter()
+    # ranks leave the host barrier up to a millisecond apart; where steps
+    # wait on each other across GPUs, a device barrier queued just before
+    # the start event makes every GPU's timed region start together
+    barrier = getattr(w, "device_barrier", None)
+    if d.world > 1 and barrier is not None:
+        barrier(s)
     e0.record(s)
     for i in range(steps):
         if i in evs:
