@@ -277,11 +277,13 @@ THORK_API int thork_ipc_close(void *d_ptr);
 
 /* thork_skinny_gemm_bf16 with flags.  THORK_SKINNY_W_STATIC promises that
  * no kernel launched earlier on the stream writes W (decode weights): the
- * stream-K kernel (M <= 32) then fetches W for its opening pipeline stages
- * before its programmatic-dependent-launch wait, overlapping the previous
- * kernel's tail.  X and Y keep the full stream ordering.  Larger M ignores
- * the flag (its 192 KiB pipeline leaves no room for the next launch on an
- * SM, measured no faster).  No reference counterpart.                     */
+ * stream-K kernels (M <= 32, and M <= 64 when the 128-column tiles fill
+ * at most half of the SMs) then fetch W for their opening pipeline stages
+ * before the programmatic-dependent-launch wait, overlapping the previous
+ * kernel's tail.  X and Y keep the full stream ordering.  The one-CTA-per-
+ * tile kernel of larger M ignores the flag (its 192 KiB pipeline leaves no
+ * room for the next launch on an SM, measured no faster).  No reference
+ * counterpart.                                                            */
 #define THORK_SKINNY_W_STATIC 1
 THORK_API int thork_skinny_gemm_bf16_ex(const void *d_x, const void *d_w, void *d_y, int M, int N,
                                         int K, int flags, void *stream);

@@ -253,7 +253,8 @@ enum KernelId {
   K_GEMM_BF16 = 0, K_GEMM_E4M3, K_SKINNY64, K_SKINNY128, K_SKINNY256,
   K_GEMM2_BF16, K_GEMM2_E4M3, K_SKSK16, K_SKSK32, K_GEMM_BF16_SK, K_GEMM_E4M3_SK,
   K_AG_BF16, K_AGP_BF16, K_AG_E4M3, K_AGP_E4M3,  // fused all-gather: staged, push warps
-  K_AGM_BF16, K_AGM_E4M3                         // fused all-gather through a multicast view
+  K_AGM_BF16, K_AGM_E4M3,                        // fused all-gather through a multicast view
+  K_SKSK64                                       // stream-K decode, M 33..64, few tiles
 };
 
 template <class Cfg, int AG = AG_NONE>
@@ -701,7 +702,17 @@ extern "C" int thork_skinny_gemm_bf16_ex(const void *d_x, const void *d_w, void 
   // per 128-column tile
   if (M <= 16) return run_skinny_sk<CfgSkinny16>(K_SKSK16, d_x, d_w, d_y, M, N, K, s, w_static);
   if (M <= 32) return run_skinny_sk<CfgSkinny32>(K_SKSK32, d_x, d_w, d_y, M, N, K, s, w_static);
-  if (M <= 64) return run_skinny<CfgSkinny64>(K_SKINNY64, d_x, d_w, d_y, M, N, K, s);
+  if (M <= 64) {
+    // few 128-column tiles (W split over GPUs): stream-K keeps every SM
+    // streaming (measured K=4096: N=3584 18.9 vs 27.5 us, N=1792 21.9 vs
+    // 27.4); with many tiles one CTA per tile is faster (N=14336: 28.4 vs
+    // 33.1 us).  For M > 64 the wider fp32 partials lose either way.
+    int sms;
+    if ((rc = thork_sm_count(&sms))) return rc;
+    if (prefer_stream_k((N + CfgSkinny64::BM - 1) / CfgSkinny64::BM, sms))
+      return run_skinny_sk<CfgSkinny64>(K_SKSK64, d_x, d_w, d_y, M, N, K, s, w_static);
+    return run_skinny<CfgSkinny64>(K_SKINNY64, d_x, d_w, d_y, M, N, K, s);
+  }
   if (M <= 128) return run_skinny<CfgSkinny128>(K_SKINNY128, d_x, d_w, d_y, M, N, K, s);
   if (M <= 256) return run_skinny<CfgSkinny256>(K_SKINNY256, d_x, d_w, d_y, M, N, K, s);
   return thork_set_error(THORK_ERR_INVALID, "skinny_gemm_bf16: M must be <= 256 (M=%d)", M);
