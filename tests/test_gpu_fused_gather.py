@@ -262,3 +262,72 @@ def test_fused_gemm_allgather_through_multicast():
         p.join(timeout=300)
     results = dict(q.get(timeout=10) for _ in range(world))
     assert results == {r: "ok" for r in range(world)}, results
+
+
+def _rank_auto_fallback(rank, world, port, q):
+    """mode="auto" with an injected multicast set-up failure on rank 1: every
+    rank falls back to P2P stores together and the results stay right."""
+    import datetime
+    import torch.distributed as td
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), THORK_FAULT_MC_SETUP="1")
+    td.init_process_group("gloo", rank=rank, world_size=world,
+                          timeout=datetime.timedelta(seconds=60))
+    comm = fg = None
+    try:
+        import thork_b200 as tk
+        from thork_b200 import dist
+        from oracle import oracle
+        rt = tk.runtime
+        rt.set_device(rank)
+        uid = [None]
+        if rank == 0:
+            import ctypes
+            buf = (ctypes.c_uint8 * 128)()
+            rt.check(rt.lib().thork_nccl_get_unique_id(buf))
+            uid = [bytes(buf)]
+        td.broadcast_object_list(uid, src=0)
+        comm = dist.Communicator(rank, world, unique_id=uid[0])
+        m, n, k = 1024, 512, 256
+        fg = dist.FusedGather(comm, m, n, mode="auto")
+        a, b = oracle.gemm_inputs(m, n, k, seed=51)
+        a16, b16 = oracle.f32_to_bf16_bits(a), oracle.f32_to_bf16_bits(b)
+        s, e = dist.row_shard(m, world, rank)
+        stream = rt.Stream()
+        got = fg.matmul(rt.to_device(np.ascontiguousarray(a16[s:e])), rt.to_device(b16),
+                        stream).to_host(stream=stream)
+        err = oracle.max_rel_err(oracle.bf16_bits_to_f32(got), oracle.gemm_bf16_ref(a16, b16))
+        mode = fg.mode
+        fg.close()
+        fg = None
+        q.put((rank, "ok" if mode == "p2p" and err <= 1e-2 else f"mode {mode} err {err}"))
+    except Exception as exc:  # noqa: BLE001 - reported to the parent
+        q.put((rank, repr(exc)))
+    finally:
+        if fg is not None:
+            fg.close()
+        if comm is not None:
+            comm.close()
+        td.destroy_process_group()
+
+
+def test_auto_mode_falls_back_to_p2p_together():
+    import thork_b200 as tk
+    from thork_b200 import dist
+    ndev = tk.runtime.device_count()
+    if ndev < 3:
+        pytest.skip("needs 3 GPUs (auto takes multicast from three ranks)")
+    tk.runtime.set_device(0)
+    if not dist.multicast_supported():
+        pytest.skip("NVLink multicast not supported here")
+    world = min(ndev, 8)
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_auto_fallback, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    results = dict(q.get(timeout=10) for _ in range(world))
+    assert results == {r: "ok" for r in range(world)}, results

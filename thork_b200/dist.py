@@ -168,6 +168,11 @@ def receive_fd(name: str, timeout: float = 60.0):
             cli.close()
 
 
+class MulticastSetupError(RuntimeError):
+    """Setting up a multicast buffer failed on some rank; every rank of the
+    group raises it together (after releasing what it held)."""
+
+
 class _Multicast:
     """This rank's part of an NVLink multicast buffer (``thork_mc_*``): one
     object for the group, this GPU's memory bound to it, an ordinary view
@@ -205,9 +210,13 @@ class _Multicast:
         except Exception as e:  # noqa: BLE001 - decided together below
             err = e
         self._step(agree, err, "share the multicast object")
-        self._step(agree, self._try(lambda: rt.check(L.thork_mc_add_device(self.obj),
-                                                     "multicast add device")),
-                   "add every device")
+        def add():
+            # host-side fault injection for tests: this rank fails to add its
+            # device, after every rank holds the object and before any binds
+            if os.environ.get("THORK_FAULT_MC_SETUP", "") == str(rank):
+                raise RuntimeError("injected multicast set-up failure (THORK_FAULT_MC_SETUP)")
+            rt.check(L.thork_mc_add_device(self.obj), "multicast add device")
+        self._step(agree, self._try(add), "add every device")
 
         def bind():
             local, multi = ctypes.c_void_p(), ctypes.c_void_p()
@@ -231,8 +240,8 @@ class _Multicast:
         if agree(err is None):
             return
         self.release()
-        raise RuntimeError(f"multicast buffer: could not {what} on every rank"
-                           + (f" (this rank: {err})" if err is not None else ""))
+        raise MulticastSetupError(f"multicast buffer: could not {what} on every rank"
+                                  + (f" (this rank: {err})" if err is not None else ""))
 
     def release(self) -> None:
         if self.obj:
@@ -278,7 +287,8 @@ class FusedGather:
     GPU's outgoing NVLink traffic and store count do not grow with the
     number of peers.  Only the flag page is exchanged through CUDA IPC.
     ``mode="auto"`` takes multimem for three or more ranks when every GPU
-    supports it, else p2p.
+    supports it, else p2p, and falls back to p2p (on every rank together)
+    when setting up the multicast buffer fails.
 
     Results rotate through the slots: consume a call's result (stream-ordered
     on this rank) before making the next call.  Requires one GPU per rank
@@ -308,6 +318,18 @@ class FusedGather:
             # at two ranks both ways measured the same; from three on, one
             # multicast store per line beats a store per peer
             mode = "multimem" if flag.to_host()[0] == self.world and self.world >= 3 else "p2p"
+            try:
+                self._setup(mode)
+            except MulticastSetupError:
+                # every rank saw the same failure (agreed): fall back together
+                self._setup("p2p")
+            return
+        self._setup(mode)
+
+    def _setup(self, mode: str) -> None:
+        L = rt.lib()
+        comm = self.comm
+        self.mc = None
         self.mode = mode
         # p2p: the slots and the flag page in one IPC-shared allocation;
         # multimem: only the flag page is shared through IPC
