@@ -796,86 +796,117 @@ __global__ void __launch_bounds__(192, 1)
         const int lt = tile - sp.dp_tiles;  // tile index within the stream-K units
         const int first = sk_cta_of_unit(lt * nkb, sp.base, sp.extra);
         const int nseg = sk_cta_of_unit((lt + 1) * nkb - 1, sp.base, sp.extra) - first + 1;
-        const int slot = sk_slot(blockIdx.x, lt, nkb, sp.base, sp.extra);
-        // slot layout [BN/4][BM] float4: a warp's 32 rows of one 4-column
-        // chunk are 512 contiguous bytes, for both this write and the fixup
-        float4 *mine = reinterpret_cast<float4 *>(sp.partial) +
-                       (static_cast<long long>(blockIdx.x) * 2 + slot) * (Cfg::BN / 4) * Cfg::BM + row;
-        constexpr int CH = (Cfg::BN % 32 == 0) ? 32 : 16;
+        constexpr int V = Cfg::BN / 4;
+        constexpr int VC = V < 8 ? V : 8;  // float4 per chunk: 16 or 32 columns
+        constexpr int CH = 4 * VC;
+        if (k0 != 0) {
+          // not the tile's head segment: this CTA's fp32 partial goes to its
+          // slot ([BN/4][BM] float4: a warp's 32 rows of one 4-column chunk
+          // are 512 contiguous bytes), then it counts itself in
+          const int slot = sk_slot(blockIdx.x, lt, nkb, sp.base, sp.extra);
+          float4 *mine = reinterpret_cast<float4 *>(sp.partial) +
+                         (static_cast<long long>(blockIdx.x) * 2 + slot) * V * Cfg::BM + row;
 #pragma unroll 1
-        for (int c0 = 0; c0 < Cfg::BN; c0 += CH) {
-          u32 r[CH];
-          if constexpr (CH == 32)
-            tmem_ld_32x32b_x32(t_row + c0, r);
-          else
-            tmem_ld_32x32b_x16(t_row + c0, r);
-          tmem_wait_ld();
+          for (int c0 = 0; c0 < Cfg::BN; c0 += CH) {
+            u32 r[CH];
+            if constexpr (CH == 32)
+              tmem_ld_32x32b_x32(t_row + c0, r);
+            else
+              tmem_ld_32x32b_x16(t_row + c0, r);
+            tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < CH / 4; ++j)
-            mine[(c0 / 4 + j) * Cfg::BM] =
-                make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                            __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-        }
-        __threadfence();
-        epi_bar();
-        if (threadIdx.x == 64) {
-          const unsigned old = atomicAdd(sp.counters + tile, 1u);
-          *last_flag = (old == static_cast<unsigned>(nseg - 1)) ? 1u : 0u;
-        }
-        epi_bar();
-        if (*last_flag) {
+            for (int j = 0; j < CH / 4; ++j)
+              mine[(c0 / 4 + j) * Cfg::BM] =
+                  make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                              __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+          }
           __threadfence();
-          // sum the covering CTAs' slots in CTA order, 32 columns at a time;
-          // all loads of a slot's chunk are in flight at once
-          constexpr int V = Cfg::BN / 4;
-          constexpr int VC = V < 8 ? V : 8;
-#pragma unroll 1
-          for (int c = 0; c < V; c += VC) {
-            float4 sum[VC];
-#pragma unroll
-            for (int j = 0; j < VC; ++j) sum[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int sgi = 0; sgi < nseg; ++sgi) {
-              const int cta = first + sgi;
-              const float4 *slot4 =
-                  reinterpret_cast<const float4 *>(sp.partial) +
-                  (static_cast<long long>(cta) * 2 + sk_slot(cta, lt, nkb, sp.base, sp.extra)) * V * Cfg::BM +
-                  row;
-              float4 v[VC];
-#pragma unroll
-              for (int j = 0; j < VC; ++j) v[j] = __ldcg(slot4 + (c + j) * Cfg::BM);
-#pragma unroll
-              for (int j = 0; j < VC; ++j) {
-                sum[j].x += v[j].x;
-                sum[j].y += v[j].y;
-                sum[j].z += v[j].z;
-                sum[j].w += v[j].w;
+          epi_bar();
+          if (threadIdx.x == 64) atomicAdd(sp.counters + tile, 1u);
+        } else {
+          // the head segment (k-blocks from 0) is the last range its CTA
+          // works on, so it sums the tile: once the other nseg - 1 segments
+          // have counted themselves in (bounded wait), its own accumulator
+          // from TMEM plus their slots in CTA order -- the order every split
+          // tile has always been summed in
+          if (threadIdx.x == 64) {
+            u32 ok = 1;
+            const u64 t0 = globaltimer();
+            for (;;) {
+              unsigned v;
+              asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(sp.counters + tile)
+                           : "memory");
+              if (v >= static_cast<unsigned>(nseg - 1)) break;
+              if (*abort_flag || globaltimer() - t0 > THORK_WAIT_TIMEOUT_NS) {
+                if (!*abort_flag) report_status(p.status, STATUS_WAIT_TIMEOUT, 0x27);
+                ok = 0;
+                break;
               }
             }
-            const float *f = reinterpret_cast<const float *>(sum);
-            if constexpr (Cfg::TRANS_OUT) {
-              if (n < p.out_cols) {
+            *last_flag = ok;
+          }
+          epi_bar();
+          if (!*last_flag) {
+            *abort_flag = 1;
+          } else {
+            __threadfence();
+#pragma unroll 1
+            for (int c = 0; c < V; c += VC) {
+              u32 r[CH];
+              if constexpr (CH == 32)
+                tmem_ld_32x32b_x32(t_row + 4 * c, r);
+              else
+                tmem_ld_32x32b_x16(t_row + 4 * c, r);
+              tmem_wait_ld();
+              float4 sum[VC];
 #pragma unroll
-                for (int m = 0; m < 4 * VC; ++m)
-                  if (4 * c + m < p.out_rows)
-                    st_global_b16(out + static_cast<long long>(4 * c + m) * p.ldo + n,
-                                  pack_bf16x2(f[m] * p.alpha, 0.0f));
+              for (int j = 0; j < VC; ++j)
+                sum[j] = make_float4(0.f + __uint_as_float(r[4 * j]), 0.f + __uint_as_float(r[4 * j + 1]),
+                                     0.f + __uint_as_float(r[4 * j + 2]),
+                                     0.f + __uint_as_float(r[4 * j + 3]));
+              for (int sgi = 1; sgi < nseg; ++sgi) {
+                const int cta = first + sgi;
+                const float4 *slot4 =
+                    reinterpret_cast<const float4 *>(sp.partial) +
+                    (static_cast<long long>(cta) * 2 + sk_slot(cta, lt, nkb, sp.base, sp.extra)) * V * Cfg::BM +
+                    row;
+                float4 v[VC];
+#pragma unroll
+                for (int j = 0; j < VC; ++j) v[j] = __ldcg(slot4 + (c + j) * Cfg::BM);
+#pragma unroll
+                for (int j = 0; j < VC; ++j) {
+                  sum[j].x += v[j].x;
+                  sum[j].y += v[j].y;
+                  sum[j].z += v[j].z;
+                  sum[j].w += v[j].w;
+                }
               }
-            } else if (n < p.out_rows) {
-              // row n of C, columns tn*BN + 4c .. + 4 VC, 16-byte stores
+              const float *f = reinterpret_cast<const float *>(sum);
+              if constexpr (Cfg::TRANS_OUT) {
+                if (n < p.out_cols) {
 #pragma unroll
-              for (int g = 0; g < VC / 2; ++g) {
-                const int col = tn * Cfg::BN + 4 * c + 8 * g;
-                if (col < p.out_cols) {
-                  u32 w[4];
+                  for (int m = 0; m < 4 * VC; ++m)
+                    if (4 * c + m < p.out_rows)
+                      st_global_b16(out + static_cast<long long>(4 * c + m) * p.ldo + n,
+                                    pack_bf16x2(f[m] * p.alpha, 0.0f));
+                }
+              } else if (n < p.out_rows) {
+                // row n of C, columns tn*BN + 4c .. + 4 VC, 16-byte stores
 #pragma unroll
-                  for (int h = 0; h < 4; ++h)
-                    w[h] = pack_bf16x2(f[8 * g + 2 * h] * p.alpha, f[8 * g + 2 * h + 1] * p.alpha);
-                  st_global_v4(out + static_cast<long long>(n) * p.ldo + col, w[0], w[1], w[2], w[3]);
+                for (int g = 0; g < VC / 2; ++g) {
+                  const int col = tn * Cfg::BN + 4 * c + 8 * g;
+                  if (col < p.out_cols) {
+                    u32 w[4];
+#pragma unroll
+                    for (int h = 0; h < 4; ++h)
+                      w[h] = pack_bf16x2(f[8 * g + 2 * h] * p.alpha, f[8 * g + 2 * h + 1] * p.alpha);
+                    st_global_v4(out + static_cast<long long>(n) * p.ldo + col, w[0], w[1], w[2], w[3]);
+                  }
                 }
               }
             }
+            if (threadIdx.x == 64) sp.counters[tile] = 0u;  // ready for the next launch
           }
-          if (threadIdx.x == 64) sp.counters[tile] = 0u;  // ready for the next launch
         }
         epi_bar();
       }
