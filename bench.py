@@ -938,10 +938,11 @@ def also_measurements(args, d, rt, dist_mod, peaks, main=None, sampler=None, ms_
     out["traced_tile_gemm_4096"] = traced_tile_gemm(tk, rt, peaks)
     for ncta in (1, 2):
         out[f"traced_tile_matmul_4096_{ncta}cta"] = traced_tile_matmul(tk, rt, peaks, ncta)
+    out["traced_tile_matmul_4096_persistent"] = traced_tile_matmul(tk, rt, peaks, 1, persistent=True)
     return out
 
 
-def traced_tile_matmul(tk, rt, peaks, ncta, size=4096):
+def traced_tile_matmul(tk, rt, peaks, ncta, size=4096, persistent=False):
     """tk.kernels.tile_matmul: the warp-specialised tcgen05 pipeline written
     with tk.kittens (1-CTA 128x256 tiles, or cluster pairs with
     cta_group::2 256x256 tiles), device-resident, CUDA-event timed."""
@@ -950,10 +951,11 @@ def traced_tile_matmul(tk, rt, peaks, ncta, size=4096):
     A = rt.to_device(bf16_bits(rng.standard_normal((m, k), dtype=np.float32)))
     B = rt.to_device(bf16_bits(rng.standard_normal((k, n), dtype=np.float32)))
     D = rt.empty((m, n), np.uint16)
-    mm = tk.kernels.tile_matmul(m, n, k, ncta=ncta)
+    mm = tk.kernels.tile_matmul(m, n, k, ncta=ncta, persistent=persistent)
     mm(D, A, B)  # trace + NVRTC compile
     out = time_traced(mm, (D, A, B), rt, 2.0 * m * n * k, peaks,
-                      f"tk.kernels.tile_matmul(ncta={ncta}): traced warp-specialised pipeline")
+                      f"tk.kernels.tile_matmul(ncta={ncta}, persistent={persistent}): traced "
+                      "warp-specialised pipeline")
     out["check"] = check_gemm_rows(D, A, B, rt)
     return out
 

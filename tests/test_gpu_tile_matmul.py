@@ -95,3 +95,22 @@ def test_prepared_launches_match_dropin_call():
     assert rt.kernel_status() == 0
     with pytest.raises(TypeError, match="DeviceArray"):
         mm.prepare(want, A, B)
+
+
+@pytest.mark.parametrize("m,n,k", [(2048, 4096, 256), (512, 512, 512), (4096, 4096, 4096)])
+def test_persistent_tile_matmul(m, n, k):
+    """The persistent form (one CTA per SM, two TMEM accumulators): several
+    tiles per CTA at 2048 x 4096 and 4096^3, bit-equal to the one-tile-per-CTA
+    form (same 128 x 256 tiles, same k order)."""
+    rt = tk.runtime
+    _, _, a16, b16 = _inputs(m, n, k, seed=m + k, scale=1.0)
+    A, B = rt.to_device(a16), rt.to_device(b16)
+    C1, C2 = rt.empty((m, n), np.uint16), rt.empty((m, n), np.uint16)
+    tk.kernels.tile_matmul(m, n, k, persistent=True)(C1, A, B)
+    tk.kernels.tile_matmul(m, n, k)(C2, A, B)
+    c1 = C1.to_host()
+    np.testing.assert_array_equal(c1, C2.to_host())
+    rows = np.sort(np.random.default_rng(6).choice(m, 64, replace=False))
+    err = oracle.max_rel_err(oracle.bf16_bits_to_f32(c1[rows]), oracle.gemm_bf16_ref(a16[rows], b16))
+    assert err <= TOL, f"max rel err {err:.3e}"
+    assert rt.kernel_status() == 0

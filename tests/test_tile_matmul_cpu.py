@@ -77,3 +77,14 @@ def test_tensor_to_shared_store_checks_shapes():
 
     with pytest.raises(TypeError, match="store\\(shared, tensor\\)"):
         bad.cuda_source
+
+
+def test_persistent_tile_matmul_compiles_and_checks_shapes():
+    mm = tk.kernels.tile_matmul(2048, 4096, 512, persistent=True)
+    kern = mm.kernel._kernel
+    assert "arrive" in mm.cuda_source and kern.dynamic_smem <= 227 * 1024
+    kern.compile_for_arch("100a")
+    with pytest.raises(ValueError):
+        tk.kernels.tile_matmul(256, 256, 192, persistent=True)  # K/64 not a multiple of 4
+    with pytest.raises(ValueError):
+        tk.kernels.tile_matmul(256, 256, 256, ncta=2, persistent=True)

@@ -175,7 +175,12 @@ __device__ __forceinline__ void wait(semaphore &s, int phase, u32 *status) {
   if (!mbar_wait(sem_addr(s), static_cast<u32>(phase & 1), status, 0x40)) abort_flag() = 1;
 }
 
-__device__ __forceinline__ void arrive(semaphore &s) { mbar_arrive(sem_addr(s)); }
+// Also orders this thread's earlier tensor-memory accesses (tcgen05.ld of an
+// accumulator being handed back) before the arrival.
+__device__ __forceinline__ void arrive(semaphore &s) {
+  tc_fence_before();
+  mbar_arrive(sem_addr(s));
+}
 
 // ------------------------------------------------------------------ warp scope
 namespace warp {
@@ -558,6 +563,7 @@ struct umma_fmt<half> {
 template <bool ACC, class T, int M, int N, int K, int KB, int NB>
 __device__ __forceinline__ void umma_ab(tt<float, M, N> &d, const st<T, M, K> &a, const st<T, KB, NB> &b,
                                         semaphore &sem) {
+  tc_fence_after();  // after the semaphore wait that handed this thread the operands
   static_assert(KB == K && NB == N, "tcgen05 operand shapes disagree");
   static_assert(M == 64 || M == 128, "tcgen05 (one CTA) needs M = 64 or 128");
   static_assert(N % 16 == 0 && N >= 16 && N <= 256, "tcgen05 N must be 16..256, a multiple of 16");
@@ -572,6 +578,7 @@ __device__ __forceinline__ void umma_ab(tt<float, M, N> &d, const st<T, M, K> &a
 template <bool ACC, class T, int M, int N, int K, int NB, int KB>
 __device__ __forceinline__ void umma_abt(tt<float, M, N> &d, const st<T, M, K> &a, const st<T, NB, KB> &b,
                                          semaphore &sem) {
+  tc_fence_after();  // after the semaphore wait that handed this thread the operands
   static_assert(KB == K && NB == N, "tcgen05 operand shapes disagree");
   static_assert(M == 64 || M == 128, "tcgen05 (one CTA) needs M = 64 or 128");
   static_assert(N % 16 == 0 && N >= 16 && N <= 256, "tcgen05 N must be 16..256, a multiple of 16");
@@ -594,6 +601,7 @@ __device__ __forceinline__ void commit_pair(semaphore &sem) {
 template <bool ACC, class T, int M, int N, int K, int KB, int NH>
 __device__ __forceinline__ void umma2_ab(tt<float, M, N> &d, const st<T, M, K> &a, const st<T, KB, NH> &b,
                                          semaphore &sem) {
+  tc_fence_after();  // after the semaphore wait that handed this thread the operands
   static_assert(KB == K && 2 * NH == N, "2-CTA tcgen05: B holds K x N/2 per CTA");
   static_assert(M == 128, "2-CTA tcgen05: 128 rows per CTA (M = 256 per pair)");
   static_assert(N % 32 == 0 && N >= 32 && N <= 256, "2-CTA tcgen05 N must be 32..256, a multiple of 32");
@@ -607,6 +615,7 @@ __device__ __forceinline__ void umma2_ab(tt<float, M, N> &d, const st<T, M, K> &
 template <bool ACC, class T, int M, int N, int K, int NH, int KB>
 __device__ __forceinline__ void umma2_abt(tt<float, M, N> &d, const st<T, M, K> &a, const st<T, NH, KB> &b,
                                           semaphore &sem) {
+  tc_fence_after();  // after the semaphore wait that handed this thread the operands
   static_assert(KB == K && 2 * NH == N, "2-CTA tcgen05: B holds N/2 x K per CTA");
   static_assert(M == 128, "2-CTA tcgen05: 128 rows per CTA (M = 256 per pair)");
   static_assert(N % 32 == 0 && N >= 32 && N <= 256, "2-CTA tcgen05 N must be 32..256, a multiple of 32");

@@ -32,7 +32,7 @@ __all__ = [
     "swap_layout", "mma_AB", "mma_AB_t", "warpgroup", "Semaphore", "semaphore",
     "init_semaphore", "wait", "tma", "TensorTile", "TensorAllocator", "tt_bf", "tt_hf",
     "tt_fl", "tensor_allocator", "tensor_alloc", "tcgen05_commit", "tensor_load_wait",
-    "cluster_ctarank", "cluster_sync",
+    "cluster_ctarank", "cluster_sync", "arrive",
 ]
 
 _ELEM = {"float32": "float", "float16": "__half", "bfloat16": "__nv_bfloat16",
@@ -348,6 +348,18 @@ def init_semaphore(sem: Semaphore, n_arrived: int, n_threads: int) -> None:
     b = current_builder()
     mark_kittens(b)
     _stmt(b, f"{NS}::init_semaphore", [sem._expr, ir.Lit(int(n_arrived)), ir.Lit(int(n_threads))])
+
+
+def arrive(sem: Semaphore) -> None:
+    """Arrive once on ``sem`` from the calling thread (ThunderKittens'
+    ``kittens::arrive``; no counterpart in the reference's front end).  Earlier
+    tensor-memory reads of the thread are ordered before the arrival, so it
+    can hand an accumulator back to the MMA issuer."""
+    if not isinstance(sem, Semaphore):
+        raise TypeError("arrive expects a kittens.semaphore handle")
+    b = current_builder()
+    mark_kittens(b)
+    _stmt(b, f"{NS}::arrive", [sem._expr])
 
 
 def wait(sem: Semaphore, phase) -> None:
