@@ -227,6 +227,23 @@ def test_skinny_stream_k_shapes(m, n, k):
     assert err <= TOL, f"max rel err {err:.3e}"
 
 
+@pytest.mark.parametrize("m,n,k", [(64, 14336, 1024), (65, 2048, 1024), (100, 1160, 768),
+                                   (128, 136, 512), (129, 4096, 640), (256, 2304, 512),
+                                   (250, 520, 1000)])
+def test_skinny_tile_shapes(m, n, k):
+    """Decode shapes served one CTA per 128-column tile (M 33..256 with many
+    tiles): ragged M leaves part of the X box out of range, ragged N part of
+    the last tile's W columns, and K = 1000 ends in a partial 64-wide K
+    block.  The output starts as NaN bits so an unwritten element fails."""
+    x, w = oracle.skinny_inputs(m, n, k, seed=9)
+    x16, w16 = oracle.f32_to_bf16_bits(x), oracle.f32_to_bf16_bits(w)
+    y16 = np.full((m, n), 0x7FC0, np.uint16)
+    tk.kernels.matmul(m, n, k, tk.dt.bfloat16, variant="skinny")(y16, x16, w16)
+    err = oracle.max_rel_err(oracle.bf16_bits_to_f32(y16), oracle.gemm_bf16_ref(x16, w16))
+    assert err <= TOL, f"max rel err {err:.3e}"
+    assert tk.runtime.kernel_status() == 0
+
+
 def test_skinny_stream_k_repeated_calls_are_identical():
     # the split tiles' arrival counters return to zero after every launch, so
     # back-to-back calls (including a different shape in between) agree

@@ -92,7 +92,8 @@ enum : int { AG_NONE = 0, AG_STAGED = 1, AG_PUSH = 2, AG_MULTIMEM = 3 };
 
 template <class Cfg, int AG>
 constexpr int gemm_smem_bytes() {
-  return (AG == AG_STAGED || AG == AG_MULTIMEM) ? Cfg::SMEM_BYTES_STAGED : Cfg::SMEM_BYTES;
+  return (AG == AG_STAGED || AG == AG_MULTIMEM || Cfg::TRANS_OUT) ? Cfg::SMEM_BYTES_STAGED
+                                                                   : Cfg::SMEM_BYTES;
 }
 template <class Cfg, int AG>
 constexpr int gemm_threads() {
@@ -179,6 +180,80 @@ __device__ __forceinline__ void bf16_store_tile(const Params &p, u32 t_row, int 
         }
       }
     }
+  }
+}
+
+// Named barrier 1 over the 128 epilogue threads.
+__device__ __forceinline__ void epi_bar() {
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+// Same barrier, returning whether any of the 128 threads passed `v` = true,
+// so all epilogue warps take the same branch.
+__device__ __forceinline__ bool epi_vote_any(bool v) {
+  u32 r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.or.pred po, 1, 128, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"(v ? 1u : 0u)
+      : "memory");
+  return r != 0;
+}
+
+// Transposed (swap-AB) epilogue of one tile, shared by the four epilogue
+// warps: TMEM lane n holds W column n0 + n, and its BN accumulator columns
+// are the tile's rows of Y.  Per 64-row slice, the two lanes of a pair swap
+// one value (shfl) so that each thread writes two adjacent columns of one
+// row as one 4-byte word into a [64][128] bf16 staging slice (256-byte
+// rows; on odd rows the 16-byte chunks are XOR 4, so a warp's even and odd
+// lanes write different banks).  After a barrier of the 128 epilogue
+// threads each warp stores 16 whole rows of the slice, two 256-byte row
+// segments per instruction, instead of one 64-byte piece of a row per
+// instruction.
+template <class Cfg>
+__device__ __forceinline__ void bf16_store_tile_trans(const Params &p, u32 t_lane, int n0, int m0,
+                                                      unsigned char *stg, int q, int lane) {
+  static_assert(Cfg::TRANS_OUT && Cfg::BM == 128 && Cfg::BN % 64 == 0, "transposed staging layout");
+  static_assert(4 * Cfg::EPI_WARP_BYTES >= 64 * 256, "staging slice is 64 rows of 256 bytes");
+  unsigned short *out = static_cast<unsigned short *>(p.out);
+  const bool odd = lane & 1;
+  const int nw = q * 32 + (lane & ~1);  // first of the two columns this thread writes
+  const int wchunk = nw >> 3;           // its 16-byte chunk of the 256-byte row
+  const int wbyte = (nw & 7) * 2;       // and the byte within the chunk
+#pragma unroll 1
+  for (int c0 = 0; c0 < Cfg::BN; c0 += 64) {
+#pragma unroll
+    for (int h = 0; h < 64; h += 32) {
+      u32 r[32];
+      tmem_ld_32x32b_x32(t_lane + c0 + h, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        // even lane: row i, columns (own, partner); odd lane: row i + 1, (partner, own)
+        const u32 got = __shfl_xor_sync(0xffffffffu, odd ? r[i] : r[i + 1], 1);
+        const float lo = __uint_as_float(odd ? got : r[i]);
+        const float hi = __uint_as_float(odd ? r[i + 1] : got);
+        const int row = h + i + (odd ? 1 : 0);
+        *reinterpret_cast<u32 *>(stg + row * 256 + ((wchunk ^ ((row & 1) << 2)) * 16) + wbyte) =
+            pack_bf16x2(lo * p.alpha, hi * p.alpha);
+      }
+    }
+    epi_bar();  // the slice is complete
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int row = q * 16 + 2 * j + (lane >> 4);
+      const int chunk = lane & 15;
+      const uint4 v =
+          *reinterpret_cast<const uint4 *>(stg + row * 256 + ((chunk ^ ((row & 1) << 2)) * 16));
+      const int orow = m0 + c0 + row, ocol = n0 + chunk * 8;
+      // N is a multiple of 8, so a 16-byte chunk is wholly in or out
+      if (orow < p.out_rows && ocol < p.out_cols)
+        st_global_v4(out + static_cast<long long>(orow) * p.ldo + ocol, v.x, v.y, v.z, v.w);
+    }
+    epi_bar();  // every warp has read the slice before the next one is written
   }
 }
 
@@ -470,15 +545,21 @@ __global__ void __launch_bounds__(gemm_threads<Cfg, AG>(), 1)
   } else {
     // ------------------------------------------------ epilogue (warps 2..5)
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    // the transposed store synchronises the four epilogue warps, so they
+    // leave the tile loop together: the abort decision is a vote of all 128
+    constexpr bool kVote = Cfg::TRANS_OUT && AG == AG_NONE;
     int it = 0;
-    for (int t = blockIdx.x; t < ntiles && !*abort_flag; t += gridDim.x, ++it) {
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+      if (!kVote && *abort_flag) break;
       int tm, tn;
       tile_coords<Cfg::GROUP_M>(t, ntm, ntn, tm, tn);
       const int acc = it & 1;
       const u32 acc_ph = (it >> 1) & 1;
-      bool ok = true;
-      if (lane == 0) ok = mbar_wait(tfull_bar(acc), acc_ph, p.status, 6);
-      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
+      bool ok = kVote ? !*abort_flag : true;
+      if (lane == 0 && ok) ok = mbar_wait(tfull_bar(acc), acc_ph, p.status, 6);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if constexpr (kVote) ok = !epi_vote_any(!ok);
+      if (!ok) {
         *abort_flag = 1;
         break;
       }
@@ -489,6 +570,8 @@ __global__ void __launch_bounds__(gemm_threads<Cfg, AG>(), 1)
         bf16_store_tile_peers<Cfg, AG == AG_MULTIMEM>(p, t_row, tm * Cfg::BM + q * 32, tn * Cfg::BN,
                                                       smem + Cfg::EPI_OFF + q * Cfg::EPI_WARP_BYTES,
                                                       lane);
+      else if constexpr (Cfg::TRANS_OUT)
+        bf16_store_tile_trans<Cfg>(p, t_row, tm * Cfg::BM, tn * Cfg::BN, smem + Cfg::EPI_OFF, q, lane);
       else
         bf16_store_tile<Cfg>(p, t_row, row_mma, tn * Cfg::BN);
       tc_fence_before();
@@ -588,26 +671,6 @@ struct SkIter {
     return true;
   }
 };
-
-// Named barrier 1 over the 128 epilogue threads.
-__device__ __forceinline__ void epi_bar() {
-  asm volatile("bar.sync 1, 128;" ::: "memory");
-}
-
-// Same barrier, returning whether any of the 128 threads passed `v` = true,
-// so all epilogue warps take the same branch.
-__device__ __forceinline__ bool epi_vote_any(bool v) {
-  u32 r;
-  asm volatile(
-      "{\n\t.reg .pred pi, po;\n\t"
-      "setp.ne.u32 pi, %1, 0;\n\t"
-      "bar.red.or.pred po, 1, 128, pi;\n\t"
-      "selp.u32 %0, 1, 0, po;\n\t}"
-      : "=r"(r)
-      : "r"(v ? 1u : 0u)
-      : "memory");
-  return r != 0;
-}
 
 template <class Cfg>
 __global__ void __launch_bounds__(192, 1)
