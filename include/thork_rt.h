@@ -277,8 +277,9 @@ THORK_API int thork_ipc_close(void *d_ptr);
 
 /* thork_skinny_gemm_bf16 with flags.  THORK_SKINNY_W_STATIC promises that
  * no kernel launched earlier on the stream writes W (decode weights): the
- * stream-K kernels (M <= 32, and M <= 64 when the 128-column tiles fill
- * at most half of the SMs) then fetch W for their opening pipeline stages
+ * stream-K kernels (M <= 32; M <= 64 when the 128-column tiles fill at
+ * most half of the SMs; M <= 128 when they fill between a sixth and a half
+ * of them) then fetch W for their opening pipeline stages
  * before the programmatic-dependent-launch wait, overlapping the previous
  * kernel's tail.  X and Y keep the full stream ordering.  The one-CTA-per-
  * tile kernel of larger M ignores the flag (its 192 KiB pipeline leaves no

@@ -217,7 +217,8 @@ def test_pipelined_host_path_ragged_chunks(dtype):
 
 @pytest.mark.parametrize("m,n,k", [(20, 14336, 4096), (32, 1024, 512), (1, 4480, 512), (3, 128, 64),
                                    (16, 2048, 8192), (48, 1792, 4096), (64, 3584, 1024),
-                                   (40, 1000, 640)])
+                                   (40, 1000, 640), (128, 7168, 4096), (100, 3584, 1024),
+                                   (65, 4096, 640), (128, 3080, 1000)])
 def test_skinny_stream_k_shapes(m, n, k):
     x, w = oracle.skinny_inputs(m, n, k, seed=5)
     x16, w16 = oracle.f32_to_bf16_bits(x), oracle.f32_to_bf16_bits(w)

@@ -254,7 +254,8 @@ enum KernelId {
   K_GEMM2_BF16, K_GEMM2_E4M3, K_SKSK16, K_SKSK32, K_GEMM_BF16_SK, K_GEMM_E4M3_SK,
   K_AG_BF16, K_AGP_BF16, K_AG_E4M3, K_AGP_E4M3,  // fused all-gather: staged, push warps
   K_AGM_BF16, K_AGM_E4M3,                        // fused all-gather through a multicast view
-  K_SKSK64                                       // stream-K decode, M 33..64, few tiles
+  K_SKSK64,                                      // stream-K decode, M 33..64, few tiles
+  K_SKSK128                                      // stream-K decode, M 65..128, few tiles
 };
 
 template <class Cfg, int AG = AG_NONE>
@@ -699,7 +700,7 @@ extern "C" int thork_skinny_gemm_bf16_ex(const void *d_x, const void *d_w, void 
   const bool w_static = (flags & THORK_SKINNY_W_STATIC) != 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // M <= 32: stream-K over all SMs (partials are small); larger M: one CTA
-  // per 128-column tile
+  // per 128-column tile unless the tiles leave most SMs idle
   if (M <= 16) return run_skinny_sk<CfgSkinny16>(K_SKSK16, d_x, d_w, d_y, M, N, K, s, w_static);
   if (M <= 32) return run_skinny_sk<CfgSkinny32>(K_SKSK32, d_x, d_w, d_y, M, N, K, s, w_static);
   if (M <= 64) {
@@ -713,7 +714,18 @@ extern "C" int thork_skinny_gemm_bf16_ex(const void *d_x, const void *d_w, void 
       return run_skinny_sk<CfgSkinny64>(K_SKSK64, d_x, d_w, d_y, M, N, K, s, w_static);
     return run_skinny<CfgSkinny64>(K_SKINNY64, d_x, d_w, d_y, M, N, K, s);
   }
-  if (M <= 128) return run_skinny<CfgSkinny128>(K_SKINNY128, d_x, d_w, d_y, M, N, K, s);
+  if (M <= 128) {
+    // stream-K again when the tiles fill between a sixth and a half of the
+    // SMs (measured K=4096, M=128: N=7168 25.0 vs 27.1 us, N=3584 24.7 vs
+    // 26.2); with fewer tiles each is split so many ways that the 64 KiB
+    // fp32 partials cost more than the idle SMs (N=1792: 32.2 vs 25.9).
+    int sms;
+    if ((rc = thork_sm_count(&sms))) return rc;
+    const int tiles = (N + CfgSkinny128::BM - 1) / CfgSkinny128::BM;
+    if (prefer_stream_k(tiles, sms) && tiles * 6 >= sms)
+      return run_skinny_sk<CfgSkinny128>(K_SKSK128, d_x, d_w, d_y, M, N, K, s, w_static);
+    return run_skinny<CfgSkinny128>(K_SKINNY128, d_x, d_w, d_y, M, N, K, s);
+  }
   if (M <= 256) return run_skinny<CfgSkinny256>(K_SKINNY256, d_x, d_w, d_y, M, N, K, s);
   return thork_set_error(THORK_ERR_INVALID, "skinny_gemm_bf16: M must be <= 256 (M=%d)", M);
 }
