@@ -52,3 +52,19 @@ def test_host_launcher_paths_explain_themselves():
         rt.compile_source_to_shared_lib("")
     with pytest.raises(NotImplementedError):
         rt.dispatch_tk(None, "k", [], [], (1, 1, 1), (1, 1, 1), 0)
+
+
+@pytest.mark.parametrize("m,chunk", [(8192, 1024), (3000, 512), (1024, 256), (2047, 256),
+                                     (5000, 768), (1500, 512), (100000, 12544)])
+def test_pipelined_host_path_chunk_schedule(m, chunk):
+    """The row chunks of the pipelined host path cover every row once, in
+    order; long inputs start and end with short chunks, short ones keep
+    equal chunks."""
+    from thork_b200.kernels._library import chunk_schedule
+    sched = chunk_schedule(m, chunk)
+    assert sum(sched) == m and min(sched) > 0 and max(sched) <= chunk
+    if m >= 4 * chunk:
+        q = chunk // 4
+        assert sched[:2] == [q, 2 * q] and sched[-3:] == [3 * q, q, q]
+    else:
+        assert sched == [min(chunk, m - r0) for r0 in range(0, m, chunk)]
