@@ -478,7 +478,7 @@ class GemmWorkload:
     def e2e_step(self, tk):
         if self.d.world == 1:
             dtype = tk.dt.bfloat16 if self.kind == "bf16" else tk.dt.float8_e4m3
-            mm = tk.kernels.matmul(self.m, self.n, self.k, dtype, variant="gemm") \
+            mm = tk.kernels.matmul(self.m, self.n, self.k, dtype, variant="gemm_auto") \
                 if self.kind == "bf16" else tk.kernels.matmul(self.m, self.n, self.k, dtype)
             if self.kind == "bf16":
                 mm(self.pc, self.pa, self.pb)

@@ -198,8 +198,9 @@ THORK_API int thork_matrix_add_f32(float *d_out, const float *d_a, const float *
  * bf16 out.  Requires K % 8 == 0 and N % 8 == 0 (16-byte TMA strides).
  * `variant` 0 = automatic, 1 = 1-CTA 128x256 tiles, 2 = 2-CTA 256x256,
  * 3 = stream-K over 128x256 tiles (whole waves one tile per CTA, the tiles
- * of the last wave split into equal k-loop shares over all SMs; chosen
- * automatically when the tiles fill at most half of the SMs).
+ * of the last wave split into equal k-loop shares over all SMs).  The
+ * automatic choice is 3 when the tiles fill at most half of the SMs, else
+ * 2 when M > 128, else 1.
  * Replaces tk.kernels.matmul (src/thork/kernels/matmul.py:17-71, fp32 SIMT
  * only) for dtype=bfloat16, and the level-06 tcgen05 matmul that
  * tests/test_kittens.py:187-274 can only compile.                          */
@@ -277,13 +278,11 @@ THORK_API int thork_ipc_close(void *d_ptr);
 
 /* thork_skinny_gemm_bf16 with flags.  THORK_SKINNY_W_STATIC promises that
  * no kernel launched earlier on the stream writes W (decode weights): the
- * stream-K kernels (M <= 32; M <= 64 when the 128-column tiles fill at
- * most half of the SMs; M <= 128 when they fill between a sixth and a half
- * of them) then fetch W for their opening pipeline stages
- * before the programmatic-dependent-launch wait, overlapping the previous
- * kernel's tail.  X and Y keep the full stream ordering.  The one-CTA-per-
- * tile kernel of larger M ignores the flag (its 192 KiB pipeline leaves no
- * room for the next launch on an SM, measured no faster).  No reference
+ * stream-K kernels (M <= 64 when the 128-column tiles fill at most half
+ * of the SMs) then fetch W for their opening pipeline stages before the
+ * programmatic-dependent-launch wait, overlapping the previous kernel's
+ * tail.  X and Y keep the full stream ordering.  The one-CTA-per-tile
+ * kernel of the other shapes ignores the flag (measured no faster).  No reference
  * counterpart.                                                            */
 #define THORK_SKINNY_W_STATIC 1
 THORK_API int thork_skinny_gemm_bf16_ex(const void *d_x, const void *d_w, void *d_y, int M, int N,

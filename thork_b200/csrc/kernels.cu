@@ -255,7 +255,7 @@ enum KernelId {
   K_AG_BF16, K_AGP_BF16, K_AG_E4M3, K_AGP_E4M3,  // fused all-gather: staged, push warps
   K_AGM_BF16, K_AGM_E4M3,                        // fused all-gather through a multicast view
   K_SKSK64,                                      // stream-K decode, M 33..64, few tiles
-  K_SKSK128                                      // stream-K decode, M 65..128, few tiles
+  K_SKINNY16, K_SKINNY32                         // one CTA per tile, M <= 32
 };
 
 template <class Cfg, int AG = AG_NONE>
@@ -332,14 +332,16 @@ extern "C" int thork_gemm_bf16(const void *d_a, const void *d_b, void *d_c, int 
   if ((rc = thork_status_word(&status))) return rc;
   Params prm{d_c, M, N, K, N, M, N, 1.0f, status};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // automatic choice: under the power cap the 1-CTA kernel sustains ~3% more
-  // on bf16 than the 2-CTA one (same-box A/B at 8192^3); stream-K when the
-  // 128 x 256 tiles would fill at most half of the SMs
+  // automatic choice: stream-K when the 128 x 256 tiles would fill at most
+  // half of the SMs; otherwise the 2-CTA kernel once a pair tile has work
+  // for both CTAs (measured 8192^3: 1447 against 1414 TFLOP/s in bursts,
+  // 1264-1269 against 1242-1249 over 2.5 s under the power cap; 4096^3:
+  // 1360 against 1280)
   if (variant == 0) {
     int sms;
     if ((rc = thork_sm_count(&sms))) return rc;
     const long long tiles = static_cast<long long>((M + C::BM - 1) / C::BM) * ((N + C::BN - 1) / C::BN);
-    variant = prefer_stream_k(tiles, sms) ? 3 : 1;
+    variant = prefer_stream_k(tiles, sms) ? 3 : (M > 128 ? 2 : 1);
   }
   if (variant == 2) return run_gemm2<Cfg2Bf16>(K_GEMM2_BF16, ta, tb, prm, s, "gemm2_bf16 launch");
   if (variant == 3) return run_gemm_sk<C>(K_GEMM_BF16_SK, ta, tb, prm, s);
@@ -698,36 +700,32 @@ extern "C" int thork_skinny_gemm_bf16_ex(const void *d_x, const void *d_w, void 
   if (flags & ~THORK_SKINNY_W_STATIC)
     return thork_set_error(THORK_ERR_INVALID, "skinny_gemm_bf16: unknown flags 0x%x", flags);
   const bool w_static = (flags & THORK_SKINNY_W_STATIC) != 0;
+  if (M > 256)
+    return thork_set_error(THORK_ERR_INVALID, "skinny_gemm_bf16: M must be <= 256 (M=%d)", M);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // M <= 32: stream-K over all SMs (partials are small); larger M: one CTA
-  // per 128-column tile unless the tiles leave most SMs idle
-  if (M <= 16) return run_skinny_sk<CfgSkinny16>(K_SKSK16, d_x, d_w, d_y, M, N, K, s, w_static);
-  if (M <= 32) return run_skinny_sk<CfgSkinny32>(K_SKSK32, d_x, d_w, d_y, M, N, K, s, w_static);
+  // One CTA per 128-column tile of W, except that M <= 64 takes stream-K
+  // when the tiles fill at most half of the SMs (W split over GPUs).
+  // Measured K=4096 (static weights): N=14336 one CTA per tile 23.2-23.6 /
+  // 23.5 / 22.8 us at M=1 / 16 / 32 against 23.9 / 24.1 / 24.9 stream-K;
+  // M=64 at N=3584 / 1792 stream-K 17.6 / 19.9 against 20.8 / 20.7; M=128
+  // at N=7168 / 3584 one CTA per tile 22.4 / 21.6 against 24.9 / 24.3.
+  int sms;
+  if ((rc = thork_sm_count(&sms))) return rc;
+  const bool few_tiles = prefer_stream_k((N + CfgSkinny16::BM - 1) / CfgSkinny16::BM, sms);
+  if (M <= 16) {
+    if (few_tiles) return run_skinny_sk<CfgSkinny16>(K_SKSK16, d_x, d_w, d_y, M, N, K, s, w_static);
+    return run_skinny<CfgSkinny16>(K_SKINNY16, d_x, d_w, d_y, M, N, K, s);
+  }
+  if (M <= 32) {
+    if (few_tiles) return run_skinny_sk<CfgSkinny32>(K_SKSK32, d_x, d_w, d_y, M, N, K, s, w_static);
+    return run_skinny<CfgSkinny32>(K_SKINNY32, d_x, d_w, d_y, M, N, K, s);
+  }
   if (M <= 64) {
-    // few 128-column tiles (W split over GPUs): stream-K keeps every SM
-    // streaming (measured K=4096: N=3584 18.9 vs 27.5 us, N=1792 21.9 vs
-    // 27.4); with many tiles one CTA per tile is faster (N=14336: 28.4 vs
-    // 33.1 us).  For M > 64 the wider fp32 partials lose either way.
-    int sms;
-    if ((rc = thork_sm_count(&sms))) return rc;
-    if (prefer_stream_k((N + CfgSkinny64::BM - 1) / CfgSkinny64::BM, sms))
-      return run_skinny_sk<CfgSkinny64>(K_SKSK64, d_x, d_w, d_y, M, N, K, s, w_static);
+    if (few_tiles) return run_skinny_sk<CfgSkinny64>(K_SKSK64, d_x, d_w, d_y, M, N, K, s, w_static);
     return run_skinny<CfgSkinny64>(K_SKINNY64, d_x, d_w, d_y, M, N, K, s);
   }
-  if (M <= 128) {
-    // stream-K again when the tiles fill between a sixth and a half of the
-    // SMs (measured K=4096, M=128: N=7168 25.0 vs 27.1 us, N=3584 24.7 vs
-    // 26.2); with fewer tiles each is split so many ways that the 64 KiB
-    // fp32 partials cost more than the idle SMs (N=1792: 32.2 vs 25.9).
-    int sms;
-    if ((rc = thork_sm_count(&sms))) return rc;
-    const int tiles = (N + CfgSkinny128::BM - 1) / CfgSkinny128::BM;
-    if (prefer_stream_k(tiles, sms) && tiles * 6 >= sms)
-      return run_skinny_sk<CfgSkinny128>(K_SKSK128, d_x, d_w, d_y, M, N, K, s, w_static);
-    return run_skinny<CfgSkinny128>(K_SKINNY128, d_x, d_w, d_y, M, N, K, s);
-  }
-  if (M <= 256) return run_skinny<CfgSkinny256>(K_SKINNY256, d_x, d_w, d_y, M, N, K, s);
-  return thork_set_error(THORK_ERR_INVALID, "skinny_gemm_bf16: M must be <= 256 (M=%d)", M);
+  if (M <= 128) return run_skinny<CfgSkinny128>(K_SKINNY128, d_x, d_w, d_y, M, N, K, s);
+  return run_skinny<CfgSkinny256>(K_SKINNY256, d_x, d_w, d_y, M, N, K, s);
 }
 
 extern "C" int thork_skinny_gemm_bf16(const void *d_x, const void *d_w, void *d_y, int M, int N,

@@ -499,14 +499,16 @@ class FusedGather:
         self._free_own()
 
 
-def _gemm_launcher(dtype: str, m: int, n: int, k: int, scale: float = 1.0) -> Callable:
+def _gemm_launcher(dtype: str, m: int, n: int, k: int, scale: float = 1.0,
+                   variant: int = 1) -> Callable:
     L = rt.lib()
-    # whole 128 x 256 tiles (variant 1), as in the fused all-gather, so both
-    # ways of gathering C produce the same bits
+    # variant 1 (whole 128 x 256 tiles, as in the fused all-gather) whenever C
+    # is gathered, so both ways of gathering C produce the same bits; the
+    # library's automatic choice (0) when nothing is gathered
     if dtype == "bf16":
-        return lambda a, b, c, s: L.thork_gemm_bf16(a, b, c, m, n, k, 1, s)
+        return lambda a, b, c, s: L.thork_gemm_bf16(a, b, c, m, n, k, variant, s)
     if dtype == "e4m3":
-        return lambda a, b, c, s: L.thork_gemm_e4m3(a, b, c, m, n, k, float(scale), 1.0, 1, s)
+        return lambda a, b, c, s: L.thork_gemm_e4m3(a, b, c, m, n, k, float(scale), 1.0, variant, s)
     raise ValueError(f"unknown GEMM dtype {dtype!r}")
 
 
@@ -529,9 +531,10 @@ def sharded_matmul(comm: Optional[Communicator], a_local: "rt.DeviceArray", b: "
     n = b.shape[1]
     if a_local.shape[0] != m_loc or b.shape[0] != k:
         raise ValueError(f"shape mismatch: A rows {a_local.shape}, B {b.shape}, shard {m_loc}")
-    launch = _gemm_launcher(dtype, m_loc, n, k, scale)
+    local_only = not gather or world == 1
+    launch = _gemm_launcher(dtype, m_loc, n, k, scale, variant=0 if local_only else 1)
     sh = stream.handle if stream else None
-    if not gather or world == 1:
+    if local_only:
         rt.check(launch(a_local.ptr, b.ptr, c_out.ptr, sh), "sharded gemm")
         if gemm_done is not None:
             gemm_done.record(stream)
